@@ -1,0 +1,98 @@
+"""ctypes binding of the C ABI in ``include/ae_b200.h`` (``ae_b200/libae_b200.so``).
+
+There is no CPU fallback: if the library is missing or the device is not a B200, the
+calls raise.  Build the library with ``python -m ae_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libae_b200.so")
+
+DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
+
+# Every entry point declared in include/ae_b200.h, with (restype, argtypes).
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_S = ctypes.c_size_t
+SIGNATURES = {
+    "smb_version": (_I, []),
+    "smb_strerror": (ctypes.c_char_p, [_I]),
+    "smb_last_cuda_error": (ctypes.c_char_p, []),
+    "smb_moe_workspace_bytes": (_S, [_I, _I, _I, _I, _I, _I]),
+    "smb_moe_splits": (_I, [_I, _I, _I]),
+    "smb_moe_route": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "smb_moe_permute": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_ffn": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_gate_up": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_down": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_combine": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
+    "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
+    "smb_moe_align_block_size": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
+    "smb_moe_topk": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "smb_moe_read_status": (_I, [_P, _S, _I, _I, _I, _I, _I, _I, _P]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """An ``smb_*`` call returned a negative status."""
+
+    def __init__(self, fn: str, code: int, detail: str = ""):
+        self.code = code
+        msg = f"{fn} failed: {strerror(code)} (code {code})"
+        if detail:
+            msg += f": {detail}"
+        super().__init__(msg)
+
+
+def load(path: str | None = None):
+    """Load the library once; raises if it is absent (no fallback path exists)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(
+                f"ae_b200 CUDA library not found at {p}; build it with `python -m ae_b200.build`")
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def exported_symbols(path: str | None = None):
+    lib = load(path)
+    return {name: hasattr(lib, name) for name in SIGNATURES}
+
+
+def strerror(code: int) -> str:
+    lib = load()
+    s = lib.smb_strerror(int(code))
+    return s.decode() if s else "?"
+
+
+def check(fn: str, code: int):
+    if code < 0:
+        detail = ""
+        if code == -5:  # SMB_ERR_CUDA
+            d = load().smb_last_cuda_error()
+            detail = d.decode() if d else ""
+        raise NativeError(fn, code, detail)
+    return code
+
+
+def call(name: str, *args):
+    lib = load()
+    return check(name, getattr(lib, name)(*args))

@@ -1,0 +1,428 @@
+// C ABI entry points: argument checks, workspace carving, TMA descriptor encoding and
+// the launch sequence route -> gate/up GEMM -> down GEMM -> combine.  Consecutive
+// launches use programmatic dependent launch so each kernel's prologue overlaps the
+// previous kernel's tail; every kernel waits for its predecessor before it touches
+// global memory.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/ae_b200.h"
+#include "kernels.h"
+
+using namespace smb;
+
+namespace {
+
+thread_local char g_last_cuda_error[256] = "";
+
+int cuda_fail(cudaError_t err) {
+  std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(err),
+                cudaGetErrorString(err));
+  return SMB_ERR_CUDA;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool sm100 = false;
+};
+
+constexpr int kMaxDevices = 64;
+
+// Per-device facts, filled once per device.
+int device_info(DeviceInfo* out) {
+  static DeviceInfo table[kMaxDevices];
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err);
+  if (dev < 0 || dev >= kMaxDevices) return SMB_ERR_CUDA;
+  int rc = SMB_OK;
+  std::call_once(flags[dev], [&] {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      rc = SMB_ERR_CUDA;
+      return;
+    }
+    table[dev].sms = sms;
+    table[dev].sm100 = (major == 10 && minor == 0);
+  });
+  if (rc != SMB_OK) return rc;
+  if (table[dev].sms == 0) return SMB_ERR_CUDA;
+  *out = table[dev];
+  return SMB_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SMB_DISABLE_PDL");
+    return !(v != nullptr && v[0] == '1');
+  }();
+  return on;
+}
+
+int elem_bytes_of(int dtype) { return (dtype == SMB_DTYPE_F16 || dtype == SMB_DTYPE_BF16) ? 2 : 0; }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_shape(int T, int E, int k, int H, int I, int dtype) {
+  if (elem_bytes_of(dtype) == 0) return SMB_ERR_DTYPE;
+  if (T < 0 || E < 1 || E > kMaxExperts || k < 1 || k > kMaxTopK || k > E) return SMB_ERR_SHAPE;
+  if (H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0) return SMB_ERR_SHAPE;
+  if (static_cast<long long>(T) * k > kMaxFlat) return SMB_ERR_SHAPE;
+  return SMB_OK;
+}
+
+int splits_for(int E, int H, int I, int* out) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != SMB_OK) return rc;
+  const char* env = std::getenv("SMB_SPLIT_K");
+  int s = choose_splits(E, H, I, di.sms);
+  if (env != nullptr) {
+    int v = std::atoi(env);
+    if (v >= 1 && v <= I / 64) s = v;
+  }
+  *out = s;
+  return SMB_OK;
+}
+
+// Carve the workspace; checks size and alignment.
+int carve(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype, WsLayout* L) {
+  int rc = check_shape(T, E, k, H, I, dtype);
+  if (rc != SMB_OK) return rc;
+  int s = 1;
+  rc = splits_for(E, H, I, &s);
+  if (rc != SMB_OK) return rc;
+  *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s);
+  if (ws == nullptr) return SMB_ERR_NULL;
+  if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
+  if (ws_bytes < L->total) return SMB_ERR_WORKSPACE;
+  return SMB_OK;
+}
+
+template <typename P>
+P* at(const void* ws, size_t off) {
+  return reinterpret_cast<P*>(reinterpret_cast<uintptr_t>(ws) + off);
+}
+
+// 2D row-major [rows, cols] tensor of 16-bit elements, box [box_rows, 64], 128B swizzle.
+int encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return SMB_ERR_TMA;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == SMB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SMB_OK : SMB_ERR_TMA;
+}
+
+int route_grid(int Tk, int sms) {
+  int g = (Tk + 7) / 8;
+  if (g < 1) g = 1;
+  if (g > sms) g = sms;
+  return g;
+}
+
+int do_route(const void* logits, int logits_dtype, const float* in_w, const int32_t* in_ids, const void* x,
+             int dtype, int T, int E, int k, int H, int I, int renorm, float* out_w, int32_t* out_ids, void* ws,
+             size_t ws_bytes, cudaStream_t stream) {
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (logits != nullptr && logits_dtype != SMB_DTYPE_F16 && logits_dtype != SMB_DTYPE_BF16 &&
+      logits_dtype != SMB_DTYPE_F32)
+    return SMB_ERR_DTYPE;
+  if (T == 0) return SMB_OK;
+  if (x == nullptr) return SMB_ERR_NULL;
+  if (logits == nullptr && (in_w == nullptr || in_ids == nullptr)) return SMB_ERR_NULL;
+  if (!aligned(x, 16)) return SMB_ERR_ALIGN;
+  DeviceInfo di;
+  rc = device_info(&di);
+  if (rc != SMB_OK) return rc;
+  if (!di.sm100) return SMB_ERR_ARCH;
+  RouteArgs a{};
+  a.logits = logits;
+  a.logits_dtype = logits_dtype;
+  a.in_w = in_w;
+  a.in_ids = in_ids;
+  a.x = x;
+  a.T = T;
+  a.E = E;
+  a.k = k;
+  a.H = H;
+  a.renormalize = renorm ? 1 : 0;
+  a.out_w = out_w;
+  a.out_ids = out_ids;
+  a.expert_off = at<int32_t>(ws, L.expert_off);
+  a.perm = at<int32_t>(ws, L.perm);
+  a.inv = at<int32_t>(ws, L.inv);
+  a.ws_w = at<float>(ws, L.w);
+  a.ws_ids = at<int32_t>(ws, L.ids);
+  a.xp = at<void>(ws, L.xp);
+  a.status = at<int>(ws, L.status);
+  const int Tk = T * k;
+  const int grid = route_grid(Tk, di.sms);
+  a.rows_per_cta = (Tk + grid - 1) / grid;
+  cudaError_t err = launch_route(a, elem_bytes_of(dtype), grid, stream, pdl_enabled());
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+// stage bit 1: gate/up GEMM (+SiLU*mul), bit 2: down GEMM (split-K partials)
+int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k,
+           int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int stages) {
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (T == 0) return SMB_OK;
+  if (pool == nullptr || page_of_expert == nullptr) return SMB_ERR_NULL;
+  if (!aligned(pool, 16)) return SMB_ERR_ALIGN;
+  if (num_pages < 1) return SMB_ERR_SHAPE;
+  const long long rows1 = static_cast<long long>(num_pages) * 3 * I;
+  const long long rows2 = static_cast<long long>(num_pages) * 3 * H;
+  if (rows1 >= (1LL << 31) || rows2 >= (1LL << 31)) return SMB_ERR_SHAPE;
+  DeviceInfo di;
+  rc = device_info(&di);
+  if (rc != SMB_OK) return rc;
+  if (!di.sm100) return SMB_ERR_ARCH;
+  const bool bf16 = dtype == SMB_DTYPE_BF16;
+  const bool pdl = pdl_enabled();
+
+  FfnArgs args{};
+  args.expert_off = at<int32_t>(ws, L.expert_off);
+  args.page_of_expert = page_of_expert;
+  args.status = at<int>(ws, L.status);
+  args.num_pages = num_pages;
+  args.E = E;
+  args.H = H;
+  args.I = I;
+  args.Tk = T * k;
+  args.splits = L.splits;
+  const void* xp = at<void>(ws, L.xp);
+  const void* a2 = at<void>(ws, L.a2);
+
+  if (stages & 1) {
+    CUtensorMap w, b64, b32, b16;
+    if ((rc = encode_2d(&w, pool, dtype, rows1, H, 64)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b64, xp, dtype, L.rows, H, 64)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b32, xp, dtype, L.rows, H, 32)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b16, xp, dtype, L.rows, H, 16)) != SMB_OK) return rc;
+    args.out = at<void>(ws, L.a2);
+    const int units = ffn_units(kGateUp, E, H, I, 1);
+    const int grid = units < di.sms ? units : di.sms;
+    cudaError_t err = launch_ffn_gemm(kGateUp, bf16, grid, stream, pdl, w, b64, b32, b16, args);
+    if (err != cudaSuccess) return cuda_fail(err);
+  }
+  if (stages & 2) {
+    CUtensorMap w, b64, b32, b16;
+    if ((rc = encode_2d(&w, pool, dtype, rows2, I, 128)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b64, a2, dtype, L.rows, I, 64)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b32, a2, dtype, L.rows, I, 32)) != SMB_OK) return rc;
+    if ((rc = encode_2d(&b16, a2, dtype, L.rows, I, 16)) != SMB_OK) return rc;
+    args.out = at<void>(ws, L.part);
+    const int units = ffn_units(kDown, E, H, I, L.splits);
+    const int grid = units < di.sms ? units : di.sms;
+    cudaError_t err = launch_ffn_gemm(kDown, bf16, grid, stream, pdl, w, b64, b32, b16, args);
+    if (err != cudaSuccess) return cuda_fail(err);
+  }
+  return SMB_OK;
+}
+
+int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
+               cudaStream_t stream) {
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (T == 0) return SMB_OK;
+  if (out == nullptr) return SMB_ERR_NULL;
+  if (!aligned(out, 16)) return SMB_ERR_ALIGN;
+  CombineArgs a{};
+  a.part = at<const float>(ws, L.part);
+  a.inv = at<const int32_t>(ws, L.inv);
+  a.w = at<const float>(ws, L.w);
+  a.out = out;
+  a.T = T;
+  a.k = k;
+  a.H = H;
+  a.splits = L.splits;
+  cudaError_t err = launch_combine(a, dtype == SMB_DTYPE_BF16, stream, pdl_enabled());
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+}  // namespace
+
+extern "C" {
+
+int smb_version(void) { return 100; }
+
+const char* smb_strerror(int code) {
+  switch (code) {
+    case SMB_OK: return "ok";
+    case SMB_ERR_SHAPE: return "unsupported size (need H%128==0, I%64==0, 1<=E<=256, 1<=k<=min(E,8), T*k<=16384)";
+    case SMB_ERR_DTYPE: return "unsupported dtype (storage f16/bf16; logits f16/bf16/f32)";
+    case SMB_ERR_ALIGN: return "misaligned pointer (tensors 16 B, workspace 256 B)";
+    case SMB_ERR_WORKSPACE: return "workspace smaller than smb_moe_workspace_bytes";
+    case SMB_ERR_CUDA: return "CUDA runtime error (see smb_last_cuda_error)";
+    case SMB_ERR_TMA: return "tensor-map encoding failed";
+    case SMB_ERR_ARCH: return "current device is not sm_100 (B200)";
+    case SMB_ERR_NULL: return "required pointer is NULL";
+    case SMB_ERR_DEVICE_TIMEOUT: return "device pipeline wait exceeded its budget";
+    case SMB_ERR_BAD_PAGE: return "page_of_expert entry outside [0, num_pages)";
+    case SMB_ERR_BAD_EXPERT: return "expert id outside [0, E)";
+    default: return "unknown error";
+  }
+}
+
+const char* smb_last_cuda_error(void) { return g_last_cuda_error; }
+
+size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype) {
+  if (check_shape(T, E, k, H, I, dtype) != SMB_OK) return 0;
+  int s = 1;
+  if (splits_for(E, H, I, &s) != SMB_OK) return 0;
+  return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s).total;
+}
+
+int smb_moe_splits(int E, int H, int I) {
+  if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0) return SMB_ERR_SHAPE;
+  int s = 1;
+  int rc = splits_for(E, H, I, &s);
+  return rc == SMB_OK ? s : rc;
+}
+
+int smb_moe_route(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
+                  int H, int I, int renormalize, float* topk_weights, int32_t* topk_ids, void* ws,
+                  size_t ws_bytes, smb_stream_t stream) {
+  if (router_logits == nullptr && T > 0) return SMB_ERR_NULL;
+  return do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize,
+                  topk_weights, topk_ids, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, const void* x, int dtype, int T, int E,
+                    int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if ((topk_weights == nullptr || topk_ids == nullptr) && T > 0) return SMB_ERR_NULL;
+  return do_route(nullptr, SMB_DTYPE_F32, topk_weights, topk_ids, x, dtype, T, E, k, H, I, 0, nullptr, nullptr,
+                  ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int smb_moe_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
+                int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+                reinterpret_cast<cudaStream_t>(stream), 3);
+}
+
+int smb_moe_gate_up(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
+                    int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+                reinterpret_cast<cudaStream_t>(stream), 1);
+}
+
+int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
+                 int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+                reinterpret_cast<cudaStream_t>(stream), 2);
+}
+
+int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
+                    smb_stream_t stream) {
+  return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,
+                    int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H, int I,
+                    int renormalize, void* out, float* topk_weights, int32_t* topk_ids, void* ws,
+                    size_t ws_bytes, smb_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = smb_moe_route(router_logits, logits_dtype, x, dtype, T, E, k, H, I, renormalize, topk_weights,
+                         topk_ids, ws, ws_bytes, stream);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
+}
+
+int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32_t* topk_ids, const void* pool,
+                           int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H,
+                           int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = smb_moe_permute(topk_weights, topk_ids, x, dtype, T, E, k, H, I, ws, ws_bytes, stream);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
+}
+
+int smb_moe_align_block_size(const int32_t* topk_ids, int numel, int E, int block_size, int32_t* sorted_ids,
+                             int32_t* expert_ids, int32_t* num_tokens_post_pad, smb_stream_t stream) {
+  if (numel < 0 || E < 1 || E > 4096 || block_size < 1) return SMB_ERR_SHAPE;
+  if (sorted_ids == nullptr || expert_ids == nullptr || num_tokens_post_pad == nullptr) return SMB_ERR_NULL;
+  if (numel > 0 && topk_ids == nullptr) return SMB_ERR_NULL;
+  const long long max_padded = static_cast<long long>(numel) + static_cast<long long>(E) * (block_size - 1);
+  if (max_padded >= (1LL << 31)) return SMB_ERR_SHAPE;
+  const int max_blocks = static_cast<int>((max_padded + block_size - 1) / block_size);
+  cudaError_t err = launch_align(topk_ids, numel, E, block_size, sorted_ids, expert_ids, num_tokens_post_pad,
+                                 max_blocks, reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_topk(const void* router_logits, int logits_dtype, int T, int E, int k, int renormalize,
+                 float* topk_weights, int32_t* topk_ids, smb_stream_t stream) {
+  if (T < 0 || E < 1 || E > kMaxExperts || k < 1 || k > kMaxTopK || k > E) return SMB_ERR_SHAPE;
+  if (logits_dtype != SMB_DTYPE_F16 && logits_dtype != SMB_DTYPE_BF16 && logits_dtype != SMB_DTYPE_F32)
+    return SMB_ERR_DTYPE;
+  if (T == 0) return SMB_OK;
+  if (router_logits == nullptr || topk_weights == nullptr || topk_ids == nullptr) return SMB_ERR_NULL;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != SMB_OK) return rc;
+  if (!di.sm100) return SMB_ERR_ARCH;
+  cudaError_t err = launch_topk(router_logits, logits_dtype, T, E, k, renormalize ? 1 : 0, topk_weights, topk_ids,
+                                reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype,
+                        smb_stream_t stream) {
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  int h = 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaMemcpyAsync(&h, at<const int>(ws, L.status), sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return cuda_fail(err);
+  switch (h) {
+    case kDevOk: return SMB_OK;
+    case kDevTimeout: return SMB_ERR_DEVICE_TIMEOUT;
+    case kDevBadPage: return SMB_ERR_BAD_PAGE;
+    case kDevBadExpertId: return SMB_ERR_BAD_EXPERT;
+    default: return SMB_ERR_CUDA;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,139 @@
+// Weighted combine back to token order, and the block-padded permutation.
+//
+// combine: out[t, h] = sum_j w[t, j] * sum_s part[s][inv[t*k+j]][h], summed in that fixed
+// order in fp32 and rounded once to the storage dtype.  The reference applies the
+// routing weight in the down-projection epilogue (specmoe/layers/fused_moe_kernel.py:197-201)
+// and sums the k slots with torch.sum into hidden_states (:344-347); here the weight is
+// applied while the split-K partials are reduced, which keeps the result deterministic.
+//
+// align: the moe_align_block_size contract (specmoe/layers/fused_moe_kernel.py:16-85):
+// flat ids sorted by expert (ascending flat index inside an expert), each expert padded
+// to a multiple of block_size with the value numel, expert id per block, padded total.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace smb {
+
+namespace {
+
+constexpr int kCombineThreads = 256;
+
+template <typename TO>
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  const int t = blockIdx.y;
+  const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
+  if (h4 * 4 >= a.H) return;
+  const size_t Tk = static_cast<size_t>(a.T) * a.k;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < a.k; ++j) {
+    const size_t f = static_cast<size_t>(t) * a.k + j;
+    const int p = a.inv[f];
+    const float wj = a.w[f];
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(a.part + (sp * Tk + p) * a.H) + h4);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    acc.x += wj * s.x;
+    acc.y += wj * s.y;
+    acc.z += wj * s.z;
+    acc.w += wj * s.w;
+  }
+  TO* out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H + static_cast<size_t>(h4) * 4;
+  union {
+    TO h[4];
+    uint2 u;
+  } pack;
+  pack.h[0] = from_f32<TO>(acc.x);
+  pack.h[1] = from_f32<TO>(acc.y);
+  pack.h[2] = from_f32<TO>(acc.z);
+  pack.h[3] = from_f32<TO>(acc.w);
+  *reinterpret_cast<uint2*>(out) = pack.u;
+}
+
+constexpr int kAlignThreads = 1024;
+
+__global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids, int numel, int E, int block,
+                                                                int32_t* sorted_ids, int32_t* expert_ids,
+                                                                int32_t* num_post_pad, int max_blocks) {
+  extern __shared__ int32_t sm[];
+  int32_t* s_cnt = sm;          // [E]
+  int32_t* s_off = sm + E;      // [E+1]
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += kAlignThreads) s_cnt[e] = 0;
+  __syncthreads();
+  for (int f = tid; f < numel; f += kAlignThreads) {
+    const int e = ids[f];
+    if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = acc;
+      acc += (s_cnt[e] + block - 1) / block * block;
+    }
+    s_off[E] = acc;
+  }
+  const int max_padded = numel + E * (block - 1);
+  for (int i = tid; i < max_padded; i += kAlignThreads) sorted_ids[i] = numel;
+  for (int b = tid; b < max_blocks; b += kAlignThreads) expert_ids[b] = -1;
+  __syncthreads();
+  for (int e = tid; e < E; e += kAlignThreads) {
+    for (int b = s_off[e] / block; b < s_off[e + 1] / block; ++b) expert_ids[b] = e;
+    s_cnt[e] = s_off[e];  // running write position
+  }
+  if (tid == 0) num_post_pad[0] = s_off[E];
+  __syncthreads();
+  if (tid < 32) {
+    const int lane = tid;
+    for (int base = 0; base < numel; base += 32) {
+      const int f = base + lane;
+      int e = (f < numel) ? ids[f] : -1;
+      const bool act = e >= 0 && e < E;
+      const int key = act ? e : E + lane;
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int bpos = act ? s_cnt[e] : 0;
+      if (act) sorted_ids[bpos + rank] = f;
+      __syncwarp();
+      if (act && lane == __ffs(peers) - 1) s_cnt[e] = bpos + __popc(peers);
+      __syncwarp();
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream, bool pdl) {
+  const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&combine_kernel<__half>);
+  cudaLaunchConfig_t cfg = {};
+  const int h4 = a.H / 4;
+  cfg.gridDim = dim3((h4 + kCombineThreads - 1) / kCombineThreads, a.T);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<CombineArgs*>(&a)};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+cudaError_t launch_align(const int32_t* ids, int numel, int E, int block, int32_t* sorted_ids, int32_t* expert_ids,
+                         int32_t* num_post_pad, int max_blocks, cudaStream_t stream) {
+  const size_t smem = sizeof(int32_t) * (2 * static_cast<size_t>(E) + 1);
+  align_kernel<<<1, kAlignThreads, smem, stream>>>(ids, numel, E, block, sorted_ids, expert_ids, num_post_pad,
+                                                  max_blocks);
+  return cudaGetLastError();
+}
+
+}  // namespace smb

@@ -1,0 +1,72 @@
+// Workspace layout and launch-shape choices shared by the host launchers.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace smb {
+
+constexpr int kMaxExperts = 256;   // router keeps up to 8 logits per lane
+constexpr int kMaxTopK = 8;
+constexpr int kMaxFlat = 16384;    // T*k limit of the single-pass permutation
+constexpr size_t kAlign = 256;
+
+// Status codes written to the device status word (first error wins).
+enum DeviceStatus : int {
+  kDevOk = 0,
+  kDevTimeout = 1,      // an mbarrier wait ran past its budget
+  kDevBadPage = 2,      // page_of_expert[e] outside [0, P)
+  kDevBadExpertId = 3,  // a given expert id outside [0, E)
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device scratch for one layer call.  Every buffer is owned by the caller (one
+// contiguous allocation); the library only carves it.
+struct WsLayout {
+  size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert
+  size_t status;      // int32 [8]     device status word(s)
+  size_t perm;        // int32 [Tk]    perm[p] = flat slot f = t*k + j at position p
+  size_t inv;         // int32 [Tk]    inv[f] = p
+  size_t w;           // fp32  [Tk]    routing weight of flat slot f
+  size_t ids;         // int32 [Tk]    expert of flat slot f
+  size_t xp;          // elem  [rows, H] token rows in expert-major order
+  size_t a2;          // elem  [rows, I] silu(x W1^T) * (x W3^T) in expert-major order
+  size_t part;        // fp32  [S, Tk, H] split-K partials of the down projection
+  size_t total;
+  int rows;           // padded row count of xp / a2
+  int splits;         // S
+};
+
+inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes, int splits) {
+  WsLayout L{};
+  const size_t Tk = static_cast<size_t>(T) * static_cast<size_t>(k);
+  L.rows = static_cast<int>(align_up(Tk, 64) + 64);
+  L.splits = splits;
+  size_t o = 0;
+  L.expert_off = o; o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
+  L.status = o;     o = align_up(o + sizeof(int32_t) * 8, kAlign);
+  L.perm = o;       o = align_up(o + sizeof(int32_t) * Tk, kAlign);
+  L.inv = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
+  L.w = o;          o = align_up(o + sizeof(float) * Tk, kAlign);
+  L.ids = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
+  L.xp = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * H, kAlign);
+  L.a2 = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * I, kAlign);
+  L.part = o;       o = align_up(o + sizeof(float) * static_cast<size_t>(splits) * Tk * H, kAlign);
+  L.total = o;
+  return L;
+}
+
+// Split-K factor of the down projection: enough (expert, 128-row tile, split) units
+// for about two per SM when every expert is touched, never more splits than 64-wide
+// K blocks.
+inline int choose_splits(int E, int H, int I, int num_sms) {
+  const int tiles = E * (H / 128);
+  int s = (2 * num_sms + tiles - 1) / tiles;
+  const int kb = I / 64;
+  if (s < 1) s = 1;
+  if (s > kb) s = kb;
+  return s;
+}
+
+}  // namespace smb

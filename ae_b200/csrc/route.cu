@@ -1,0 +1,298 @@
+// Router + permutation + token gather, one launch.
+//
+// Reference semantics:
+//  * routing = sglang select_experts as called at specmoe/layers/FusedMoE.py:174-185
+//    (softmax over E in fp32, top-k, optional renormalisation; weights fp32, ids int32);
+//  * permutation = the moe_align_block_size contract of
+//    specmoe/layers/fused_moe_kernel.py:19-55 without the block padding: flat slots
+//    f = t*k + j bucketed by expert, ascending f inside an expert.
+//
+// Every CTA recomputes the routing of all T tokens (one warp per token, logits in
+// registers, warp-shuffle argmax with ties to the lower expert) and the expert-major
+// positions (per-warp histograms, a scan, then match_any ranks inside 32-slot chunks).
+// For verify-sized batches this costs a few kilobytes of L2 reads per CTA and removes
+// every inter-CTA dependency.  Each CTA then owns a contiguous range of flat slots:
+// it writes their routing outputs and copies their token rows into the expert-major
+// buffer xp that the gate/up GEMM streams with TMA.
+#include <cfloat>
+#include <climits>
+
+#include "../../include/ae_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace smb {
+
+namespace {
+
+constexpr int kRouteThreads = 512;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr unsigned kFull = 0xffffffffu;
+
+template <typename TL>
+__device__ __forceinline__ float logit_at(const void* base, size_t idx) {
+  return to_f32<TL>(reinterpret_cast<const TL*>(base)[idx]);
+}
+
+// Top-k of one token's logits by one warp.  Lane j < k ends with (id_j, w_j).
+template <typename TL>
+__device__ __forceinline__ void route_token(const void* logits, int t, int E, int k, int renorm, int lane,
+                                            int& my_id, float& my_w) {
+  float v[kMaxExperts / 32];
+  const size_t row = static_cast<size_t>(t) * E;
+  float m = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < kMaxExperts / 32; ++r) {
+    const int e = lane + 32 * r;
+    v[r] = (e < E) ? logit_at<TL>(logits, row + e) : -INFINITY;
+    m = fmaxf(m, v[r]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxExperts / 32; ++r) {
+    const int e = lane + 32 * r;
+    if (e < E) s += expf(v[r] - m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  const float inv_s = 1.0f / s;
+
+  unsigned taken = 0;
+  float sel_sum = 0.f;
+  my_id = -1;
+  my_w = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int be = INT_MAX;
+#pragma unroll
+    for (int r = 0; r < kMaxExperts / 32; ++r) {
+      const int e = lane + 32 * r;
+      if (e < E && !((taken >> r) & 1u) && (be == INT_MAX || v[r] > bv)) {
+        bv = v[r];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, bv, o);
+      const int oe = __shfl_xor_sync(kFull, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if (lane == (be & 31)) taken |= 1u << (be >> 5);
+    const float p = expf(bv - m) * inv_s;
+    sel_sum += p;
+    if (lane == j) {
+      my_id = be;
+      my_w = p;
+    }
+  }
+  if (renorm && lane < k) my_w = my_w / sel_sum;
+}
+
+template <typename TL>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a, int vec_per_row) {
+  extern __shared__ int32_t sm[];
+  const int Tk = a.T * a.k;
+  const int E = a.E;
+  int32_t* s_ids = sm;                                   // [Tk]
+  int32_t* s_pos = s_ids + Tk;                           // [Tk]
+  float* s_w = reinterpret_cast<float*>(s_pos + Tk);     // [Tk]
+  int32_t* s_cnt = reinterpret_cast<int32_t*>(s_w + Tk); // [warps][E]
+  int32_t* s_off = s_cnt + kRouteWarps * E;              // [E+1]
+  __shared__ int s_bad;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  if (tid == 0) {
+    s_bad = 0;
+    if (blockIdx.x == 0 && a.status != nullptr) a.status[0] = 0;
+  }
+  __syncthreads();
+
+  // 1. routing of every token (or the given routing)
+  if (a.logits != nullptr) {
+    for (int t = warp; t < a.T; t += kRouteWarps) {
+      int id;
+      float w;
+      route_token<TL>(a.logits, t, E, a.k, a.renormalize, lane, id, w);
+      if (lane < a.k) {
+        s_ids[t * a.k + lane] = id;
+        s_w[t * a.k + lane] = w;
+      }
+    }
+  } else {
+    for (int f = tid; f < Tk; f += kRouteThreads) {
+      int id = a.in_ids[f];
+      if (id < 0 || id >= E) {
+        s_bad = 1;
+        id = 0;
+      }
+      s_ids[f] = id;
+      s_w[f] = a.in_w[f];
+    }
+  }
+  for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] = 0;
+  __syncthreads();
+  if (tid == 0 && s_bad && blockIdx.x == 0) record_status(a.status, kDevBadExpertId);
+
+  // 2. per-warp histograms over contiguous flat segments
+  const int seg = (Tk + kRouteWarps - 1) / kRouteWarps;
+  const int f0 = min(Tk, warp * seg);
+  const int f1 = min(Tk, f0 + seg);
+  for (int f = f0 + lane; f < f1; f += 32) atomicAdd(&s_cnt[warp * E + s_ids[f]], 1);
+  __syncthreads();
+
+  // 3. scan: per expert over warps, then over experts
+  for (int e = tid; e < E; e += kRouteThreads) {
+    int run = 0;
+    for (int w = 0; w < kRouteWarps; ++w) {
+      const int c = s_cnt[w * E + e];
+      s_cnt[w * E + e] = run;
+      run += c;
+    }
+    s_off[e] = run;  // total for now
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // exclusive scan of E totals by one warp, 8 experts per lane at most
+    int vals[kMaxExperts / 32];
+    int local = 0;
+#pragma unroll
+    for (int r = 0; r < kMaxExperts / 32; ++r) {
+      const int e = lane * (kMaxExperts / 32) + r;
+      vals[r] = (e < E) ? s_off[e] : 0;
+      local += vals[r];
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - local;
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < kMaxExperts / 32; ++r) {
+      const int e = lane * (kMaxExperts / 32) + r;
+      if (e < E) s_off[e] = run;
+      run += vals[r];
+    }
+    if (lane == 31) s_off[E] = incl;
+  }
+  __syncthreads();
+  for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] += s_off[i % E];
+  __syncthreads();
+
+  // 4. positions, in ascending flat order inside each expert
+  for (int base = f0; base < f1; base += 32) {
+    const int f = base + lane;
+    const bool act = f < f1;
+    const int e = act ? s_ids[f] : E + lane;  // distinct keys for idle lanes
+    const unsigned peers = __match_any_sync(kFull, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    const int bpos = act ? s_cnt[warp * E + e] : 0;
+    if (act) s_pos[f] = bpos + rank;
+    __syncwarp();
+    if (act && lane == leader) s_cnt[warp * E + e] = bpos + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // 5. outputs for this CTA's flat range
+  if (blockIdx.x == 0) {
+    for (int e = tid; e <= E; e += kRouteThreads) a.expert_off[e] = s_off[e];
+  }
+  const int g0 = min(Tk, static_cast<int>(blockIdx.x) * a.rows_per_cta);
+  const int g1 = min(Tk, g0 + a.rows_per_cta);
+  for (int f = g0 + tid; f < g1; f += kRouteThreads) {
+    const int p = s_pos[f];
+    a.perm[p] = f;
+    a.inv[f] = p;
+    a.ws_w[f] = s_w[f];
+    a.ws_ids[f] = s_ids[f];
+    if (a.out_w != nullptr) a.out_w[f] = s_w[f];
+    if (a.out_ids != nullptr) a.out_ids[f] = s_ids[f];
+  }
+  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
+  uint4* xdst = reinterpret_cast<uint4*>(a.xp);
+  for (int f = g0 + warp; f < g1; f += kRouteWarps) {
+    const uint4* src = xsrc + static_cast<size_t>(f / a.k) * vec_per_row;
+    uint4* dst = xdst + static_cast<size_t>(s_pos[f]) * vec_per_row;
+    for (int i = lane; i < vec_per_row; i += 32) dst[i] = __ldg(src + i);
+  }
+}
+
+// Routing only (select_experts): one warp per token.
+template <typename TL>
+__global__ void __launch_bounds__(256) topk_kernel(const void* logits, int T, int E, int k, int renorm,
+                                                   float* out_w, int32_t* out_ids) {
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  int id;
+  float w;
+  route_token<TL>(logits, t, E, k, renorm, lane, id, w);
+  if (lane < k) {
+    out_w[static_cast<size_t>(t) * k + lane] = w;
+    out_ids[static_cast<size_t>(t) * k + lane] = id;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int k, int renorm, float* out_w,
+                        int32_t* out_ids, cudaStream_t stream) {
+  const int grid = (T + 7) / 8;
+  switch (logits_dtype) {
+    case SMB_DTYPE_F16: topk_kernel<__half><<<grid, 256, 0, stream>>>(logits, T, E, k, renorm, out_w, out_ids); break;
+    case SMB_DTYPE_BF16:
+      topk_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(logits, T, E, k, renorm, out_w, out_ids);
+      break;
+    default: topk_kernel<float><<<grid, 256, 0, stream>>>(logits, T, E, k, renorm, out_w, out_ids); break;
+  }
+  return cudaGetLastError();
+}
+
+size_t route_smem_bytes(int T, int E, int k) {
+  const size_t Tk = static_cast<size_t>(T) * k;
+  return sizeof(int32_t) * (3 * Tk + static_cast<size_t>(kRouteWarps) * E + E + 1);
+}
+
+cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStream_t stream, bool pdl) {
+  const void* fn = nullptr;
+  switch (a.logits == nullptr ? SMB_DTYPE_F32 : a.logits_dtype) {
+    case SMB_DTYPE_F16: fn = reinterpret_cast<const void*>(&route_kernel<__half>); break;
+    case SMB_DTYPE_BF16: fn = reinterpret_cast<const void*>(&route_kernel<__nv_bfloat16>); break;
+    default: fn = reinterpret_cast<const void*>(&route_kernel<float>); break;
+  }
+  const size_t smem = route_smem_bytes(a.T, a.E, a.k);
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * elem_bytes / 16);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<RouteArgs*>(&a), &vec_per_row};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+}  // namespace smb

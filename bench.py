@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""MoE verify-layer throughput on B200 (SpecMoE FusedMoE path), one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2-256] [--impl reference]
+
+A step is one pass of the MoE layer (route, gate/up GEMM + SiLU*mul, down GEMM, combine)
+over one verify batch of T synthetic tokens, inputs resident in HBM.  The timed region
+is K back-to-back steps between CUDA events on the launching stream, bracketed by a
+barrier and a device synchronise, max over ranks.  Expert weights (2.8 GB for
+Mixtral-8x7B) are far larger than the 126 MB L2, so consecutive steps do not reuse
+weights from L2.
+
+N > 1: every rank holds all experts and runs its own batch of T tokens (data-parallel
+replicas of the layer, weak scaling, no collective on the data path).
+
+Extra keys: roofline (dominant kernel = gate/up GEMM, HBM bound), cpu_baseline (the CPU
+oracle port of the reference's arithmetic on this host), e2e (FusedMoE.forward with host
+inputs copied in and the output copied out every step), clocks, gpu_launches, kernels
+(per-kernel µs from a staged pass), sweep (other verify batch sizes).
+
+``--impl reference``: rank 0 times the reference's arithmetic on the host cores (the
+reference has no CPU expert path of its own; its Triton GPU kernel is the GPU side), the
+other ranks exit without work.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE verify-layer tokens/sec"
+UNIT = "tokens/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while work runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 9:
+                continue
+            self.rows.append((time.time(), parts))
+
+    def mark(self):
+        return time.time()
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [p for (t, p) in self.rows if t0 <= t <= t1]
+        if self.uuid:
+            mine = [p for p in rows if self.uuid in p[0] or p[0] in self.uuid]
+            rows = mine or rows
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(p[1]) for p in rows if p[1].replace(".", "").isdigit()]
+        smax = [float(p[2]) for p in rows if p[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for p in rows:
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(float(p[3]) for p in rows if p[3].replace(".", "").isdigit())
+                if any(p[3].replace(".", "").isdigit() for p in rows) else None}
+
+
+def device_uuid(dev):
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------- CPU arm
+
+def cpu_port_time(cfg, seed: int, max_seconds: float = 20.0, max_reps: int = 5, pool_cpu=None, x=None,
+                  logits=None):
+    """Time the CPU oracle port of the layer (routing + bf16-storage expert FFN) on all host
+    threads.  Returns (tokens_per_s, seconds_per_layer, threads, reps)."""
+    from oracle import moe_oracle as mo  # the CPU baseline leg is the one bench leg allowed to use it
+    from ae_b200 import configs
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if pool_cpu is None:
+        pool_cpu = configs.make_pool(cfg, "cpu", seed=seed)
+    if x is None:
+        x, logits = configs.make_inputs(cfg, "cpu", seed=seed)
+    pages = torch.arange(cfg.E)
+
+    def one():
+        w, ids = mo.select_experts(logits, cfg.k, cfg.renormalize)
+        return mo.stack_fused_moe(x, pool_cpu, pages, w, ids, compute_dtype=torch.bfloat16)
+
+    one()  # warm-up (thread pool, page faults)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max_reps and (time.perf_counter() - t_start) < max_seconds:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return cfg.T / med, med, threads, len(times)
+
+
+def run_reference_arm(args, cfg, rank):
+    if rank != 0:
+        return
+    from ae_b200 import configs
+    torch.manual_seed(0)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    pool_cpu = configs.make_pool(cfg, "cpu", seed=0)
+    x, logits = configs.make_inputs(cfg, "cpu", seed=0)
+    from oracle import moe_oracle as mo
+    pages = torch.arange(cfg.E)
+
+    def step():
+        w, ids = mo.select_experts(logits, cfg.k, cfg.renormalize)
+        mo.stack_fused_moe(x, pool_cpu, pages, w, ids, compute_dtype=torch.bfloat16)
+
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    budget = 150.0
+    steps, warm = args.steps, args.warmup
+    if one * (steps + warm) > budget:
+        steps = max(1, int(budget / one) - 1)
+        warm = 1
+    for _ in range(max(0, warm - 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    el = time.perf_counter() - t0
+    value = cfg.T * steps / el
+    sample = (f"{steps} full layer calls of {cfg.T} tokens (all {cfg.E} experts, bf16 storage, fp32 accumulate "
+              f"in torch CPU GEMMs) on {threads} host threads")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": steps, "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "T": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU expert path (FusedMoE.forward_cpu is unreachable); this arm runs the "
+                "oracle's CPU restatement of stack_fused_moe + select_experts",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU arm
+
+def algorithmic(cfg, touched: int, Tk: int, splits: int):
+    H, I, T, E = cfg.H, cfg.I, cfg.T, cfg.E
+    gate_up = touched * 2 * I * H * 2 + Tk * H * 2 + Tk * I * 2
+    down = touched * H * I * 2 + Tk * I * 2 + splits * Tk * H * 4
+    layer = touched * 3 * H * I * 2 + 2 * T * H * 2 + T * E * 2
+    flops = 6 * H * I * Tk
+    return gate_up, down, layer, flops
+
+
+def timed_steps(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / 1000.0
+
+
+def load_traffic(cfg_key):
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(cfg_key)
+    except Exception:
+        return None
+
+
+def run_ours(args, cfg, rank, world, dev):
+    import torch.distributed as dist
+    from ae_b200 import configs, ops
+    from ae_b200.layers.FusedMoE import FusedMoE
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    stream = torch.cuda.current_stream(dev)
+    pool = configs.make_pool(cfg, dev, seed=rank)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=rank)
+    out = torch.empty_like(x)
+    Tk = cfg.T * cfg.k
+
+    def step():
+        ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out)
+
+    # warm-up and clock soak
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    t_soak = time.time()
+    soak_end = t_soak + args.soak
+    while time.time() < soak_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize(dev)
+
+    # timed region
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    elapsed = timed_steps(step, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t_timed_end = time.time()
+    el = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+    elapsed = float(el.item())
+    clocks = sampler.summary(t_soak, t_timed_end)
+    sampler.stop()
+    if not torch.isfinite(out.float()).all():
+        raise RuntimeError("non-finite layer output")
+
+    # staged pass: per-kernel durations (events between the four launches)
+    L = ops.StagedLayer(cfg.T, cfg.E, cfg.k, cfg.H, cfg.I, x.dtype, dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.staged_steps)]
+    for i in range(3):
+        L.route(logits, x, cfg.renormalize)
+        L.gate_up(pool, pages)
+        L.down(pool, pages)
+        L.combine(out)
+    for e in evs:
+        e[0].record(stream)
+        L.route(logits, x, cfg.renormalize)
+        e[1].record(stream)
+        L.gate_up(pool, pages)
+        e[2].record(stream)
+        L.down(pool, pages)
+        e[3].record(stream)
+        L.combine(out)
+        e[4].record(stream)
+    torch.cuda.synchronize(dev)
+    names = ["route", "gate_up", "down", "combine"]
+    kern_us = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs) * 1000.0 for i, n in enumerate(names)}
+    v = L.views()
+    off = v["expert_off"].cpu()
+    touched = int(((off[1:] - off[:-1]) > 0).sum())
+    splits = ops.splits(cfg.E, cfg.H, cfg.I)
+    gu_bytes, dn_bytes, layer_bytes, flops = algorithmic(cfg, touched, Tk, splits)
+
+    # end to end through the drop-in module: host inputs in, host output out, every step
+    moe = FusedMoE(cfg.E, cfg.k, cfg.H, cfg.I, params_dtype=x.dtype, renormalize=cfg.renormalize, tp_size=1)
+    moe.ws.gpu_cache = pool
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    dx = torch.empty_like(x)
+    dl = torch.empty_like(logits)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        r = moe(dx, dl, pages)
+        hout.copy_(r, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e2e_el = timed_steps(e2e_step, args.steps, stream)
+    t = torch.tensor([e2e_el], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_el = float(t.item())
+
+    # other verify batch sizes of the same layer (rank 0 view, N=1 only)
+    sweep = {}
+    if world == 1 and not args.no_sweep:
+        for Ts in args.sweep:
+            if Ts == cfg.T:
+                continue
+            xs, ls = configs.make_inputs(cfg, dev, seed=1, T=Ts)
+            os_ = torch.empty_like(xs)
+
+            def s():
+                ops.moe_forward(xs, ls, pool, pages, cfg.k, cfg.renormalize, out=os_)
+
+            for _ in range(5):
+                s()
+            torch.cuda.synchronize(dev)
+            n = max(10, args.steps // 2)
+            el_s = timed_steps(s, n, stream)
+            us = el_s / n * 1e6
+            sweep[f"T{Ts}"] = {"us_per_layer": round(us, 2), "tokens_per_s": round(Ts / (el_s / n), 1),
+                               "layer_hbm_frac": round(algorithmic(
+                                   configs.MoEConfig(cfg.name, cfg.H, cfg.I, cfg.E, cfg.k, Ts, cfg.router_std),
+                                   cfg.E, Ts * cfg.k, splits)[2] / (el_s / n) / 1e9 / hbm_peak, 4)}
+
+    # CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        pool_cpu = pool.cpu()
+        tps, sec, threads, reps = cpu_port_time(cfg, 0, pool_cpu=pool_cpu, x=x.cpu(), logits=logits.cpu())
+        cpu = {"value": round(tps, 2), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{reps} full layer calls of {cfg.T} tokens ({cfg.name}), median {sec * 1000:.1f} ms, "
+                         f"oracle CPU restatement, bf16 storage / fp32 accumulate, {threads} threads"}
+        del pool_cpu
+
+    if rank != 0:
+        return
+    step_s = elapsed / args.steps
+    gu_s = kern_us["gate_up"] * 1e-6
+    achieved = gu_bytes / gu_s / 1e9
+    traffic = load_traffic(args.config)
+    line = {
+        "metric": METRIC,
+        "value": round(world * cfg.T * args.steps / elapsed, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1000, 5),
+        "us_per_layer": round(step_s * 1e6, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: expert weights N(0,0.02) bf16, tokens N(0,1), router logits x@Wr^T "
+                f"(Wr std {cfg.router_std:.4g})",
+        "config": {"workload": cfg.name, "T": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
+                   "experts_touched": touched, "splits": splits,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (expert weights %.2f GB per step)" % (cfg.weight_bytes() / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "gate_up (ffn_gemm_kernel<1>)", "achieved": round(achieved, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_kind": peak_kind, "alg_bytes_per_launch": gu_bytes,
+                     "traffic": traffic},
+        "layer_roofline": {"alg_bytes": layer_bytes, "achieved_gbs": round(layer_bytes / step_s / 1e9, 1),
+                           "frac_hbm": round(layer_bytes / step_s / 1e9 / hbm_peak, 4),
+                           "tflops": round(flops / step_s / 1e12, 2),
+                           "frac_tensor": round(flops / step_s / 1e12 / tc_peak, 4)},
+        "kernels_us": {n: round(u, 2) for n, u in kern_us.items()},
+        "down_roofline_frac": round(dn_bytes / (kern_us["down"] * 1e-6) / 1e9 / hbm_peak, 4),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(world * cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
+                "h2d_bytes_per_step": x.numel() * x.element_size() + logits.numel() * logits.element_size(),
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "api": "ae_b200.layers.FusedMoE.FusedMoE.forward"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+        "sweep": sweep,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c2-256")
+    ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed load before timing")
+    ap.add_argument("--staged-steps", type=int, default=20)
+    ap.add_argument("--sweep", type=int, nargs="*", default=[16, 64])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    from ae_b200 import configs
+    cfg = configs.BY_KEY[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, cfg, rank)
+        return
+
+    from ae_b200 import build
+    if rank == 0:
+        build.build()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.barrier()
+    try:
+        run_ours(args, cfg, rank, world, dev)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

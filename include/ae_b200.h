@@ -1,0 +1,148 @@
+/*
+ * ae_b200 — C ABI of the B200 (sm_100a) MoE verify layer.
+ *
+ * The layer replaces the GPU expert path of SpecMoE (zzhbrr/ae):
+ *   FusedMoE.forward           specmoe/layers/FusedMoE.py:508-532
+ *   -> UnquantizedFusedMoEMethod.forward_cuda   specmoe/layers/FusedMoE.py:155-196
+ *      -> sglang select_experts                 (call at FusedMoE.py:174-185)
+ *      -> stack_fused_moe                       specmoe/layers/fused_moe_kernel.py:253-349
+ *           moe_align_block_size (:16-85), fused_moe_kernel GEMM1 (:332-335),
+ *           silu_and_mul (:337), fused_moe_kernel GEMM2 x routing weight (:339-342),
+ *           torch.sum over top-k into hidden_states (:344-349)
+ *
+ * The reference has no FFI for this path (it is Python + Triton); these entry points
+ * are what a binding of that Python surface calls.  Conventions:
+ *   - every pointer is a device pointer unless stated; the caller owns every buffer,
+ *     including the workspace (size from smb_moe_workspace_bytes); nothing here
+ *     allocates device memory;
+ *   - calls are asynchronous and ordered on `stream` (a cudaStream_t); distinct streams
+ *     may call concurrently with distinct workspaces;
+ *   - return 0 (SMB_OK) or a negative SMB_ERR_* code; nothing aborts the process;
+ *   - weights: `pool` is the expert page pool [num_pages, 3*I*H] in the page layout of
+ *     FusedMoE.weight_loader (specmoe/layers/FusedMoE.py:485-505): page = [w1 (I x H) |
+ *     w3 (I x H) | w2 (H x I)], row-major; `page_of_expert` is the int64 [E] indirection
+ *     (`expert_cache_indices`, FusedMoE.py:508; `indicies`, fused_moe_kernel.py:256);
+ *   - storage dtype SMB_DTYPE_F16 or SMB_DTYPE_BF16 for x / pool / out; router logits may
+ *     also be SMB_DTYPE_F32; routing weights are fp32 and expert ids int32 (as
+ *     select_experts returns them);
+ *   - shape limits: H % 128 == 0, I % 64 == 0, 1 <= E <= 256, 1 <= k <= min(E, 8),
+ *     T*k <= 16384, 16-byte aligned x / pool / out, 256-byte aligned workspace.
+ */
+#ifndef AE_B200_H_
+#define AE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SMB_API __attribute__((visibility("default")))
+#else
+#define SMB_API
+#endif
+
+typedef struct CUstream_st* smb_stream_t; /* same handle as cudaStream_t */
+
+enum smb_dtype { SMB_DTYPE_F16 = 0, SMB_DTYPE_BF16 = 1, SMB_DTYPE_F32 = 2 };
+
+enum smb_status {
+  SMB_OK = 0,
+  SMB_ERR_SHAPE = -1,         /* a size outside the limits above */
+  SMB_ERR_DTYPE = -2,         /* unsupported dtype code */
+  SMB_ERR_ALIGN = -3,         /* pointer alignment (TMA needs 16 B; workspace 256 B) */
+  SMB_ERR_WORKSPACE = -4,     /* workspace smaller than smb_moe_workspace_bytes */
+  SMB_ERR_CUDA = -5,          /* a CUDA runtime call failed (smb_last_cuda_error) */
+  SMB_ERR_TMA = -6,           /* tensor-map encoding failed or is unavailable */
+  SMB_ERR_ARCH = -7,          /* current device is not compute capability 10.0 */
+  SMB_ERR_NULL = -8,          /* a required pointer is NULL */
+  SMB_ERR_DEVICE_TIMEOUT = -9,/* device status: a pipeline wait exceeded its budget */
+  SMB_ERR_BAD_PAGE = -10,     /* device status: page_of_expert[e] outside [0, num_pages) */
+  SMB_ERR_BAD_EXPERT = -11    /* device status: a given expert id outside [0, E) */
+};
+
+/* Library version (major*100 + minor). */
+SMB_API int smb_version(void);
+
+/* Static description of an error code. */
+SMB_API const char* smb_strerror(int code);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+SMB_API const char* smb_last_cuda_error(void);
+
+/* Bytes of workspace one layer call needs (0 for invalid sizes).  Depends on the
+ * current device's SM count (split-K factor), so query it on the device you run on. */
+SMB_API size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype);
+
+/* Split-K factor the down projection uses for these sizes on the current device. */
+SMB_API int smb_moe_splits(int E, int H, int I);
+
+/* Router: softmax over E in fp32, top-k (ties to the lower expert index), optional
+ * renormalisation; then the expert-major permutation and the gather of token rows into
+ * the workspace.  Replaces select_experts (FusedMoE.py:174-185) + moe_align_block_size
+ * (fused_moe_kernel.py:329).  topk_weights [T,k] fp32 / topk_ids [T,k] int32 are optional
+ * outputs (NULL to skip). */
+SMB_API int smb_moe_route(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
+                  int H, int I, int renormalize, float* topk_weights, int32_t* topk_ids, void* ws,
+                  size_t ws_bytes, smb_stream_t stream);
+
+/* Routing only, sglang select_experts semantics (FusedMoE.py:174-185): topk_weights
+ * [T,k] fp32, topk_ids [T,k] int32. */
+SMB_API int smb_moe_topk(const void* router_logits, int logits_dtype, int T, int E, int k, int renormalize,
+                 float* topk_weights, int32_t* topk_ids, smb_stream_t stream);
+
+/* Permutation + gather from a routing computed elsewhere (stack_fused_moe's
+ * topk_weights / topk_ids arguments, fused_moe_kernel.py:257-259). */
+SMB_API int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, const void* x, int dtype, int T, int E,
+                    int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* Expert FFN on the permuted rows: tcgen05 gate/up GEMM with SiLU*mul epilogue, then the
+ * split-K down GEMM.  Replaces fused_moe_kernel GEMM1 + silu_and_mul + GEMM2
+ * (fused_moe_kernel.py:332-342).  Needs smb_moe_route or smb_moe_permute first. */
+SMB_API int smb_moe_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
+                int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* The two halves of smb_moe_ffn, for callers that interleave other work or time them
+ * separately: the gate/up GEMM with the SiLU*mul epilogue (fused_moe_kernel.py:332-337)
+ * and the split-K down GEMM (fused_moe_kernel.py:339-342). */
+SMB_API int smb_moe_gate_up(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
+                            int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+SMB_API int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
+                         int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* Routing-weighted combine into out [T,H] (may alias x).  Replaces the routed-weight
+ * multiply (fused_moe_kernel.py:197-201) and torch.sum over top-k (:344-349). */
+SMB_API int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
+                    smb_stream_t stream);
+
+/* Whole layer: route + ffn + combine (FusedMoE.forward, FusedMoE.py:508-532, without
+ * the tensor-parallel all-reduce).  out may alias x (the reference writes in place). */
+SMB_API int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,
+                    int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H, int I,
+                    int renormalize, void* out, float* topk_weights, int32_t* topk_ids, void* ws,
+                    size_t ws_bytes, smb_stream_t stream);
+
+/* Whole layer from a given routing (stack_fused_moe, fused_moe_kernel.py:253-349). */
+SMB_API int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32_t* topk_ids, const void* pool,
+                           int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H,
+                           int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* Block-padded layout of moe_align_block_size (fused_moe_kernel.py:16-85):
+ * sorted_ids [numel + E*(block_size-1)] (pad value numel), expert_ids
+ * [cdiv(numel + E*(block_size-1), block_size)] (-1 past the last used block),
+ * num_tokens_post_pad [1]. */
+SMB_API int smb_moe_align_block_size(const int32_t* topk_ids, int numel, int E, int block_size, int32_t* sorted_ids,
+                             int32_t* expert_ids, int32_t* num_tokens_post_pad, smb_stream_t stream);
+
+/* Synchronously read the device status word of the last layer call that used `ws`
+ * (0, SMB_ERR_DEVICE_TIMEOUT, SMB_ERR_BAD_PAGE or SMB_ERR_BAD_EXPERT). */
+SMB_API int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype,
+                        smb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AE_B200_H_ */

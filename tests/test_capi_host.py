@@ -1,0 +1,92 @@
+"""CPU-side checks of the C ABI library and the host logic (no GPU needed)."""
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    src = open(os.path.join(ROOT, "include", "ae_b200.h")).read()
+    return sorted(set(re.findall(r"SMB_API\s+[\w\s\*]+?\b(smb_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from ae_b200 import build, _native
+    build.build()
+    return _native.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from ae_b200 import _native
+    declared = _declared_symbols()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib, name), name
+    # the ctypes signature table covers the header exactly
+    assert sorted(_native.SIGNATURES) == declared
+
+
+def test_error_strings_and_version(lib):
+    from ae_b200 import _native
+    assert lib.smb_version() >= 100
+    for code in range(0, -12, -1):
+        assert _native.strerror(code) != "unknown error"
+    assert _native.strerror(-999) == "unknown error"
+
+
+def test_argument_checks_without_gpu(lib):
+    # size / dtype validation happens before any device call
+    assert lib.smb_moe_align_block_size(None, 4, 0, 4, None, None, None, None) == -1
+    assert lib.smb_moe_topk(None, 7, 1, 8, 2, 1, None, None, None) == -2
+    assert lib.smb_moe_topk(None, 1, 1, 8, 9, 1, None, None, None) == -1
+    assert lib.smb_moe_topk(None, 1, 0, 8, 2, 1, None, None, None) == 0  # T = 0: nothing to do
+    assert lib.smb_moe_splits(8, 100, 3584) == -1
+
+
+def test_no_host_fallback_in_product_path():
+    """The product package never imports the oracle."""
+    pkg = os.path.join(ROOT, "ae_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith(".py"):
+                src = open(os.path.join(dirpath, f)).read()
+                assert "oracle" not in src, f
+
+
+def test_ops_refuse_cpu_tensors(lib):
+    from ae_b200 import ops
+    x = torch.zeros(4, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.moe_forward(x, torch.zeros(4, 8), torch.zeros(8, 3 * 64 * 128, dtype=torch.bfloat16),
+                        torch.arange(8), 2)
+
+
+def test_fusedmoe_weight_loader_layout_and_tp_slicing():
+    from ae_b200.layers.FusedMoE import FusedMoE
+    E, k, H, I = 3, 2, 8, 6
+    moe = FusedMoE(E, k, H, I, params_dtype=torch.float32, tp_size=2)
+    assert moe.intermediate_size_per_partition == 3
+    w1 = torch.arange(I * H, dtype=torch.float32).view(I, H)
+    w3 = 1000 + torch.arange(I * H, dtype=torch.float32).view(I, H)
+    w2 = 5000 + torch.arange(H * I, dtype=torch.float32).view(H, I)
+    moe.weight_loader(moe.ws, w1, "experts.1.w1.weight", "w1", 1)
+    moe.weight_loader(moe.ws, w3, "experts.1.w3.weight", "w3", 1)
+    moe.weight_loader(moe.ws, w2, "experts.1.w2.weight", "w2", 1)
+    page = moe.ws.data[1]
+    Ip = 3
+    assert torch.equal(page[: Ip * H].view(Ip, H), w1[:Ip])       # rank 0 slice of rows
+    assert torch.equal(page[Ip * H: 2 * Ip * H].view(Ip, H), w3[:Ip])
+    assert torch.equal(page[2 * Ip * H:].view(H, Ip), w2[:, :Ip])  # rank 0 slice of columns
+    m = FusedMoE.make_expert_params_mapping("w1", "w2", "w3", 2)
+    assert m[0] == ("experts.ws", "experts.0.w1.weight", 0, "w1")
+    assert len(m) == 6
+
+
+def test_unsupported_options_raise():
+    from ae_b200.layers.FusedMoE import FusedMoE
+    with pytest.raises(NotImplementedError):
+        FusedMoE(4, 2, 128, 64, torch.bfloat16, tp_size=1, quant_config=object())
