@@ -94,8 +94,9 @@ def pool_geometry(pool: torch.Tensor, H: int):
     return P, page // (3 * H)
 
 
-def _status(ws: torch.Tensor, T, E, k, H, I, code, stream):
-    return _native.call("smb_moe_read_status", ws.data_ptr(), ws.numel(), T, E, k, H, I, code, stream)
+def _status(ws: torch.Tensor, T, E, k, H, I, code, stream) -> int:
+    """Device status of the last call on ``ws`` (0 or a negative SMB_ERR_* code); syncs."""
+    return int(_native.load().smb_moe_read_status(ws.data_ptr(), ws.numel(), T, E, k, H, I, code, stream))
 
 
 def moe_forward(x: torch.Tensor, router_logits: torch.Tensor, pool: torch.Tensor,
@@ -128,7 +129,7 @@ def moe_forward(x: torch.Tensor, router_logits: torch.Tensor, pool: torch.Tensor
                  pool.data_ptr(), P, page_of_expert.data_ptr(), code, T, E, top_k, H, I, int(bool(renormalize)),
                  out.data_ptr(), _ptr(topk_weights), _ptr(topk_ids), ws.data_ptr(), ws.numel(), stream)
     if DEBUG:
-        _status(ws, T, E, top_k, H, I, code, stream)
+        _native.check("smb_moe_forward (device status)", _status(ws, T, E, top_k, H, I, code, stream))
     return out
 
 
@@ -157,7 +158,7 @@ def moe_forward_routed(x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: to
                  pool.data_ptr(), P, page_of_expert.data_ptr(), code, T, E, k, H, I, out.data_ptr(),
                  ws.data_ptr(), ws.numel(), stream)
     if DEBUG:
-        _status(ws, T, E, k, H, I, code, stream)
+        _native.check("smb_moe_forward_routed (device status)", _status(ws, T, E, k, H, I, code, stream))
     return out
 
 
