@@ -295,6 +295,7 @@ const char* smb_strerror(int code) {
     case SMB_ERR_DEVICE_TIMEOUT: return "device pipeline wait exceeded its budget";
     case SMB_ERR_BAD_PAGE: return "page_of_expert entry outside [0, num_pages)";
     case SMB_ERR_BAD_EXPERT: return "expert id outside [0, E)";
+    case SMB_ERR_SCRATCH_LIMIT: return "workspace need exceeds the 64 MiB static scratch of smb_moe_forward_noalloc";
     default: return "unknown error";
   }
 }

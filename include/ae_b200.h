@@ -60,7 +60,8 @@ enum smb_status {
   SMB_ERR_NULL = -8,          /* a required pointer is NULL */
   SMB_ERR_DEVICE_TIMEOUT = -9,/* device status: a pipeline wait exceeded its budget */
   SMB_ERR_BAD_PAGE = -10,     /* device status: page_of_expert[e] outside [0, num_pages) */
-  SMB_ERR_BAD_EXPERT = -11    /* device status: a given expert id outside [0, E) */
+  SMB_ERR_BAD_EXPERT = -11,   /* device status: a given expert id outside [0, E) */
+  SMB_ERR_SCRATCH_LIMIT = -12 /* smb_moe_forward_noalloc: problem needs more than its 64 MiB scratch */
 };
 
 /* Library version (major*100 + minor). */
@@ -128,6 +129,22 @@ SMB_API int smb_moe_forward(const void* x, const void* router_logits, int logits
 SMB_API int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32_t* topk_ids, const void* pool,
                            int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H,
                            int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* smb_moe_forward without any device allocation, for callers that cannot allocate
+ * device memory at call time (a host whose allocator owns the HBM, a latency-critical
+ * path where cudaMalloc's implicit synchronisation is not allowed, a binding without a
+ * device allocator).  No counterpart in the reference: SpecMoE always allocates its
+ * intermediate caches with torch.empty per call.  The caller passes inputs and outputs
+ * only; the workspace is a library-owned static device array of 64 MiB per GPU (held
+ * until the process exits).  Sizes whose smb_moe_workspace_bytes exceed 64 MiB return
+ * SMB_ERR_SCRATCH_LIMIT (Mixtral-8x7B shapes fit up to T = 448 tokens on a
+ * 148-SM B200).  The first call
+ * on each device looks up the array's device address; make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race. */
+SMB_API int smb_moe_forward_noalloc(const void* x, const void* router_logits, int logits_dtype, const void* pool,
+                                    int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
+                                    int k, int H, int I, int renormalize, void* out, float* topk_weights,
+                                    int32_t* topk_ids, smb_stream_t stream);
 
 /* Block-padded layout of moe_align_block_size (fused_moe_kernel.py:16-85):
  * sorted_ids [numel + E*(block_size-1)] (pad value numel), expert_ids
