@@ -24,7 +24,7 @@ SIGNATURES = {
     "smb_strerror": (ctypes.c_char_p, [_I]),
     "smb_last_cuda_error": (ctypes.c_char_p, []),
     "smb_moe_workspace_bytes": (_S, [_I, _I, _I, _I, _I, _I]),
-    "smb_moe_splits": (_I, [_I, _I, _I]),
+    "smb_moe_splits": (_I, [_I, _I, _I, _I]),
     "smb_moe_route": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
     "smb_moe_permute": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_ffn": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),

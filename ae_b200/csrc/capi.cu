@@ -94,12 +94,12 @@ int check_shape(int T, int E, int k, int H, int I, int dtype) {
   return SMB_OK;
 }
 
-int splits_for(int E, int H, int I, int* out) {
+int splits_for(int E, int H, int I, int Tk, int* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc != SMB_OK) return rc;
   const char* env = std::getenv("SMB_SPLIT_K");
-  int s = choose_splits(E, H, I, di.sms);
+  int s = choose_splits(E, H, I, Tk, di.sms);
   if (env != nullptr) {
     int v = std::atoi(env);
     if (v >= 1 && v <= I / 64) s = v;
@@ -113,7 +113,7 @@ int carve(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, in
   int rc = check_shape(T, E, k, H, I, dtype);
   if (rc != SMB_OK) return rc;
   int s = 1;
-  rc = splits_for(E, H, I, &s);
+  rc = splits_for(E, H, I, T * k, &s);
   if (rc != SMB_OK) return rc;
   *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s);
   if (ws == nullptr) return SMB_ERR_NULL;
@@ -127,8 +127,53 @@ P* at(const void* ws, size_t off) {
   return reinterpret_cast<P*>(reinterpret_cast<uintptr_t>(ws) + off);
 }
 
+// Small cache of encoded tensor maps: a layer is called with the same pool and
+// workspace over and over, and encoding costs microseconds of host time per map.
+struct TmapKey {
+  const void* base;
+  int dtype;
+  uint64_t rows, cols;
+  uint32_t box_rows;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && dtype == o.dtype && rows == o.rows && cols == o.cols && box_rows == o.box_rows;
+  }
+};
+constexpr int kTmapCacheSize = 64;
+struct TmapCache {
+  std::mutex mu;
+  TmapKey keys[kTmapCacheSize];
+  CUtensorMap maps[kTmapCacheSize];
+  int used = 0;
+  int next = 0;
+};
+TmapCache g_tmaps;
+
+int encode_2d_uncached(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows);
+
 // 2D row-major [rows, cols] tensor of 16-bit elements, box [box_rows, 64], 128B swizzle.
 int encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  const TmapKey key{base, dtype, rows, cols, box_rows};
+  {
+    std::lock_guard<std::mutex> lock(g_tmaps.mu);
+    for (int i = 0; i < g_tmaps.used; ++i) {
+      if (g_tmaps.keys[i] == key) {
+        *map = g_tmaps.maps[i];
+        return SMB_OK;
+      }
+    }
+  }
+  const int rc = encode_2d_uncached(map, base, dtype, rows, cols, box_rows);
+  if (rc != SMB_OK) return rc;
+  std::lock_guard<std::mutex> lock(g_tmaps.mu);
+  const int slot = g_tmaps.used < kTmapCacheSize ? g_tmaps.used++ : (g_tmaps.next++ % kTmapCacheSize);
+  g_tmaps.keys[slot] = key;
+  g_tmaps.maps[slot] = *map;
+  return SMB_OK;
+}
+
+int encode_2d_uncached(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return SMB_ERR_TMA;
   const cuuint64_t dims[2] = {cols, rows};
@@ -187,6 +232,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.ws_ids = at<int32_t>(ws, L.ids);
   a.xp = at<void>(ws, L.xp);
   a.status = at<int>(ws, L.status);
+  a.done = at<int>(ws, L.done);
   const int Tk = T * k;
   const int grid = route_grid(Tk, di.sms);
   a.rows_per_cta = (Tk + grid - 1) / grid;
@@ -194,9 +240,10 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
-// stage bit 1: gate/up GEMM (+SiLU*mul), bit 2: down GEMM (split-K partials)
+// phase bit 1: gate/up GEMM (+SiLU*mul), bit 2: down GEMM (split-K partials); both bits
+// run both phases in one persistent launch.
 int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k,
-           int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int stages) {
+           int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases, bool counters_zeroed) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
@@ -212,46 +259,34 @@ int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, i
   if (rc != SMB_OK) return rc;
   if (!di.sm100) return SMB_ERR_ARCH;
   const bool bf16 = dtype == SMB_DTYPE_BF16;
-  const bool pdl = pdl_enabled();
+
+  CUtensorMap w13, w2;
+  if ((rc = encode_2d(&w13, pool, dtype, rows1, H, 128)) != SMB_OK) return rc;
+  if ((rc = encode_2d(&w2, pool, dtype, rows2, I, 128)) != SMB_OK) return rc;
 
   FfnArgs args{};
   args.expert_off = at<int32_t>(ws, L.expert_off);
   args.page_of_expert = page_of_expert;
   args.status = at<int>(ws, L.status);
+  args.done = at<int>(ws, L.done);
+  args.sched = at<int>(ws, L.done) + E;
+  args.xp = at<void>(ws, L.xp);
+  args.a2 = at<void>(ws, L.a2);
+  args.part = at<float>(ws, L.part);
   args.num_pages = num_pages;
   args.E = E;
   args.H = H;
   args.I = I;
   args.Tk = T * k;
   args.splits = L.splits;
-  const void* xp = at<void>(ws, L.xp);
-  const void* a2 = at<void>(ws, L.a2);
-
-  if (stages & 1) {
-    CUtensorMap w, b64, b32, b16;
-    if ((rc = encode_2d(&w, pool, dtype, rows1, H, 64)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b64, xp, dtype, L.rows, H, 64)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b32, xp, dtype, L.rows, H, 32)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b16, xp, dtype, L.rows, H, 16)) != SMB_OK) return rc;
-    args.out = at<void>(ws, L.a2);
-    const int units = ffn_units(kGateUp, E, H, I, 1);
-    const int grid = units < di.sms ? units : di.sms;
-    cudaError_t err = launch_ffn_gemm(kGateUp, bf16, grid, stream, pdl, w, b64, b32, b16, args);
+  args.phase_mask = phases;
+  if (!counters_zeroed) {
+    // standalone call: the router zeroed the counters for the first FFN launch only
+    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (E + 1), stream);
     if (err != cudaSuccess) return cuda_fail(err);
   }
-  if (stages & 2) {
-    CUtensorMap w, b64, b32, b16;
-    if ((rc = encode_2d(&w, pool, dtype, rows2, I, 128)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b64, a2, dtype, L.rows, I, 64)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b32, a2, dtype, L.rows, I, 32)) != SMB_OK) return rc;
-    if ((rc = encode_2d(&b16, a2, dtype, L.rows, I, 16)) != SMB_OK) return rc;
-    args.out = at<void>(ws, L.part);
-    const int units = ffn_units(kDown, E, H, I, L.splits);
-    const int grid = units < di.sms ? units : di.sms;
-    cudaError_t err = launch_ffn_gemm(kDown, bf16, grid, stream, pdl, w, b64, b32, b16, args);
-    if (err != cudaSuccess) return cuda_fail(err);
-  }
-  return SMB_OK;
+  cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, args);
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
 int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
@@ -305,14 +340,14 @@ const char* smb_last_cuda_error(void) { return g_last_cuda_error; }
 size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype) {
   if (check_shape(T, E, k, H, I, dtype) != SMB_OK) return 0;
   int s = 1;
-  if (splits_for(E, H, I, &s) != SMB_OK) return 0;
+  if (splits_for(E, H, I, T * k, &s) != SMB_OK) return 0;
   return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s).total;
 }
 
-int smb_moe_splits(int E, int H, int I) {
-  if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0) return SMB_ERR_SHAPE;
+int smb_moe_splits(int E, int H, int I, int Tk) {
+  if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0 || Tk < 0) return SMB_ERR_SHAPE;
   int s = 1;
-  int rc = splits_for(E, H, I, &s);
+  int rc = splits_for(E, H, I, Tk, &s);
   return rc == SMB_OK ? s : rc;
 }
 
@@ -334,19 +369,19 @@ int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, const vo
 int smb_moe_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
                 int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
   return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
-                reinterpret_cast<cudaStream_t>(stream), 3);
+                reinterpret_cast<cudaStream_t>(stream), 3, false);
 }
 
 int smb_moe_gate_up(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
                     int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
   return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
-                reinterpret_cast<cudaStream_t>(stream), 1);
+                reinterpret_cast<cudaStream_t>(stream), 1, false);
 }
 
 int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
                  int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
   return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
-                reinterpret_cast<cudaStream_t>(stream), 2);
+                reinterpret_cast<cudaStream_t>(stream), 2, false);
 }
 
 int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
@@ -362,7 +397,7 @@ int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, 
   int rc = smb_moe_route(router_logits, logits_dtype, x, dtype, T, E, k, H, I, renormalize, topk_weights,
                          topk_ids, ws, ws_bytes, stream);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3);
+  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }
@@ -373,7 +408,7 @@ int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = smb_moe_permute(topk_weights, topk_ids, x, dtype, T, E, k, H, I, ws, ws_bytes, stream);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3);
+  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }

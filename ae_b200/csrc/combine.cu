@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   for (int j = 0; j < a.k; ++j) {
     const size_t f = static_cast<size_t>(t) * a.k + j;
     const int p = a.inv[f];
+    if (p < 0 || static_cast<size_t>(p) >= Tk) continue;  // only after a failed or skipped route
     const float wj = a.w[f];
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sp = 0; sp < a.splits; ++sp) {

@@ -1,26 +1,42 @@
-// Expert FFN as two grouped, weight-streaming GEMMs on the 5th-generation tensor cores.
+// Expert FFN of the MoE layer as one persistent, weight-streaming kernel on the
+// 5th-generation tensor cores: phase 1 = gate/up GEMM with the SiLU*mul epilogue,
+// phase 2 = down GEMM (split-K), in one launch.
 //
 // Reference arithmetic: the Triton fused_moe_kernel (specmoe/layers/fused_moe_kernel.py:88-210)
 // launched twice by stack_fused_moe (:332-342) with silu_and_mul in between (:337).
 //
-// Swap-AB: in the verify regime an expert sees 1..~100 tokens, so the weight rows fill
-// the 128-row MMA M operand and the expert's tokens fill N (16..256).  Both operands
-// are K-major bf16/f16 tiles staged by TMA with the 128-byte swizzle; the fp32
-// accumulator lives in tensor memory.  One CTA per SM (persistent), warp-specialised:
-//   warp 0      TMA producer (one thread)        weights evict-first, tokens evict-last
-//   warp 1      MMA issuer (one thread)          tcgen05.mma, commits free the smem stage
-//   warp 2      TMEM allocator
+// Shape of the work.  In the verify regime an expert sees 1..~100 tokens, so the layer
+// streams the touched experts' weights once from HBM (swap-AB: weight rows fill the
+// 128-row MMA M operand, the expert's tokens fill N = 16..256).  A unit of work is 256
+// weight rows x a K range, issued as two M=128 tcgen05 MMAs per 16-wide K step that share
+// one token tile:
+//   phase 1 unit (expert, 128 features): rows of w1 (gate) and the same rows of w3 (up)
+//     from the page viewed as [P*3I, H] -> two fp32 accumulators whose lane r holds gate
+//     and up of feature r, so the epilogue forms silu(gate) * up in registers and stores
+//     the activation rows of A2 [Tk, I] (expert-major token order, storage dtype);
+//   phase 2 unit (expert, 256 hidden rows, K split): rows 2H.. of the page viewed as
+//     [P*3H, I] (the reference's w2_off) against the expert's A2 rows -> fp32 partials
+//     part[split][p][h].
+// A phase-2 unit of expert e needs every phase-1 unit of e: phase-1 epilogues count
+// their finished units per expert (release), the token loaders of phase 2 wait for the
+// count (acquire, bounded).  Every CTA runs its phase-1 units before its phase-2 units
+// and the grid is at most one CTA per SM, so the waits end.
+//
+// Data movement.  Each SM's TMA engine delivers about 50 GB/s; 148 SMs together
+// saturate HBM only if TMA moves nothing but weights.  So weights come by TMA in 16 KB
+// boxes (128 rows x 64 K, 128-byte swizzle, evict-first) and the small, L2-resident token
+// tiles come by cp.async from two loader warps, written in the same swizzled layout.
+//
+// Roles (256 threads, one CTA per SM):
+//   warp 0      TMA producer (one thread): weight boxes, 32 KB per stage
+//   warp 1      MMA issuer (one thread)
+//   warps 2, 3  token-tile loaders (64 threads, cp.async); warp 2 also owns TMEM
 //   warps 4..7  epilogue (128 threads = 128 TMEM lanes)
+// TMEM: 512 columns = two 256-column buffers (double-buffered accumulators when the
+// token tile is at most 128 wide, one buffer otherwise).
 //
-// Mode kGateUp  (GEMM1): unit = (expert, 64 intermediate features).  The A tile stacks
-//   64 rows of w1 (gate) over the matching 64 rows of w3 (up) from the page viewed as
-//   [P*3I, H]; the epilogue forms silu(gate) * up in fp32 and stores the activation
-//   row-block of A2 [Tk, I] (expert-major token order) in the storage dtype.
-// Mode kDown    (GEMM2): unit = (expert, 128 hidden rows of w2, K split).  A tile = 128
-//   rows of w2 from the page viewed as [P*3H, I] at row 2H (the w2_off of the reference),
-//   B = the expert's rows of A2; fp32 partial sums go to part[split][p][h].
-//
-// Shape limits (checked by the host): H % 128 == 0, I % 64 == 0.
+// Every wait is bounded (common.cuh); a timed-out wait records a status, unwinds and
+// releases tensor memory.
 #include <type_traits>
 
 #include "common.cuh"
@@ -31,101 +47,138 @@ namespace smb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kBK = 64;                      // K elements per stage = one 128 B swizzle row
-constexpr int kATileBytes = 128 * kBK * 2;   // 128 weight rows
-constexpr int kMaxN = 256;                   // tokens per MMA (N) and TMEM columns
-constexpr int kTmemCols = 256;
-constexpr int kMaxStages = 16;
-constexpr int kXchgFloats = 16 * 64;         // GEMM1 epilogue gate/up exchange
-constexpr int kDynSmem = 227 * 1024 - 3072;  // leaves room for the static shared block
+constexpr int kBK = 64;                        // K elements per stage = one 128 B swizzle row
+constexpr int kBoxRows = 128;                  // rows per weight box = MMA M
+constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 16 KB
+constexpr int kATileBytes = 2 * kBoxBytes;     // 256 weight rows per stage
+constexpr int kMaxN = 256;
+constexpr int kTmemCols = 512;
+constexpr int kMaxStages = 8;
+constexpr int kLoaderThreads = 64;
+constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
+constexpr int kQueueReaders = 4;               // MMA thread, the two loader-warp leaders, epilogue leader
+constexpr int kDynSmem = 227 * 1024 - 3072;
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed; the
+// arrival counts towards the phase (the barrier is initialised with one per loader).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 struct Unit {
-  int te;   // index into the touched-expert list
-  int mt;   // row tile of the weight matrix
-  int kb0;  // first 64-wide K block
-  int kb1;  // one past the last K block
-  int ks;   // split index (GEMM2)
+  int phase;  // 1 or 2
+  int te;     // index into the touched-expert list
+  int mt;     // 128-feature tile (phase 1) or 256-row tile of w2 (phase 2)
+  int kb0;    // first 64-wide K block
+  int kb1;    // one past the last K block
+  int ks;     // split index (phase 2)
 };
 
-template <int MODE>
-__device__ __forceinline__ Unit decode_unit(int u, int m_tiles, int splits, int kb_total) {
+struct Geometry {
+  int n1, n2, total;  // phase-1 units, phase-2 units, all
+  int m1, m2;         // tiles per expert
+  int kb1_total, kb2_total;
+  int splits;
+};
+
+__device__ __forceinline__ Unit decode(int u, const Geometry& g) {
   Unit r;
-  if (MODE == kGateUp) {
-    r.te = u / m_tiles;
-    r.mt = u % m_tiles;
+  if (u < g.n1) {
+    r.phase = 1;
+    r.te = u / g.m1;
+    r.mt = u % g.m1;
     r.ks = 0;
     r.kb0 = 0;
-    r.kb1 = kb_total;
+    r.kb1 = g.kb1_total;
   } else {
-    r.ks = u % splits;
-    const int q = u / splits;
-    r.te = q / m_tiles;
-    r.mt = q % m_tiles;
-    r.kb0 = static_cast<int>((static_cast<long long>(kb_total) * r.ks) / splits);
-    r.kb1 = static_cast<int>((static_cast<long long>(kb_total) * (r.ks + 1)) / splits);
+    const int v = u - g.n1;
+    r.phase = 2;
+    r.ks = v % g.splits;
+    const int q = v / g.splits;
+    r.te = q / g.m2;
+    r.mt = q % g.m2;
+    r.kb0 = static_cast<int>((static_cast<long long>(g.kb2_total) * r.ks) / g.splits);
+    r.kb1 = static_cast<int>((static_cast<long long>(g.kb2_total) * (r.ks + 1)) / g.splits);
   }
   return r;
 }
 
 }  // namespace
 
-template <int MODE, typename T>
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    ffn_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b64,
-                    const __grid_constant__ CUtensorMap tm_b32, const __grid_constant__ CUtensorMap tm_b16,
+    ffn_gemm_kernel(const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_w2,
                     const FfnArgs args) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t dyn_smem[];
-  __shared__ uint64_t full_bar[kMaxStages];
-  __shared__ uint64_t empty_bar[kMaxStages];
-  __shared__ uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ uint64_t fullA_bar[kMaxStages], fullB_bar[kMaxStages], empty_bar[kMaxStages];
+  __shared__ uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
+  __shared__ uint64_t qfull_bar[kQueue], qempty_bar[kQueue];
+  __shared__ int s_queue[kQueue];
   __shared__ uint32_t s_tmem;
   __shared__ int s_touched[kMaxExperts];
   __shared__ int s_page[kMaxExperts];
   __shared__ int s_ntouched, s_ncap, s_stages;
-  __shared__ int s_abort, s_epi_ok, s_issued, s_consumed;
+  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t raw_base = smem_u32(dyn_smem);
   const uint32_t ring_base = (raw_base + 1023u) & ~1023u;
-  uint8_t* ring_gen = dyn_smem + (ring_base - raw_base);
 
   const int E = args.E, H = args.H, I = args.I;
-  const int kb_total = (MODE == kGateUp) ? H / kBK : I / kBK;
-  const int m_tiles = (MODE == kGateUp) ? I / 64 : H / 128;
-  const int splits = (MODE == kGateUp) ? 1 : args.splits;
+  const bool do1 = (args.phase_mask & 1) != 0;
+  const bool do2 = (args.phase_mask & 2) != 0;
+  const bool chained = do1 && do2;  // phase 2 waits on this launch's phase 1
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     s_issued = 0;
     s_consumed = 0;
     for (int s = 0; s < kMaxStages; ++s) {
-      mbar_init(&full_bar[s], 1);
+      mbar_init(&fullA_bar[s], 1);
+      mbar_init(&fullB_bar[s], kLoaderThreads);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&tfull_bar, 1);
-    mbar_init(&tempty_bar, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 128);
+    }
+    for (int q = 0; q < kQueue; ++q) {
+      mbar_init(&qfull_bar[q], 1);
+      mbar_init(&qempty_bar[q], kQueueReaders);
+    }
     mbar_init(&drain_bar, 1);
     fence_mbarrier_init();
   }
   if (threadIdx.x == 32) {
-    prefetch_tmap(&tm_w);
-    prefetch_tmap(&tm_b64);
-    prefetch_tmap(&tm_b32);
-    prefetch_tmap(&tm_b16);
+    prefetch_tmap(&tm_w13);
+    prefetch_tmap(&tm_w2);
   }
   if (warp == 2) {
     tmem_alloc(&s_tmem, kTmemCols);
     tmem_relinquish();
   }
 
-  // Everything above touched only this CTA's own shared and tensor memory; the
-  // routing results and token rows come from the previous kernels in the stream.
+  // Everything above touched only this CTA's own shared and tensor memory; the routing
+  // results and the token rows come from the router launched just before.
   pdl_wait_prior_grids();
 
   if (threadIdx.x == 0) {
@@ -133,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = 0; e < E; ++e) {
       const int n = args.expert_off[e + 1] - args.expert_off[e];
       if (n > 0) {
-        long long pg = args.page_of_expert[e];
+        const long long pg = args.page_of_expert[e];
         if (pg < 0 || pg >= args.num_pages) {
           record_status(args.status, kDevBadPage);
           continue;
@@ -147,10 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ncap = (maxn + 15) & ~15;
     ncap = max(16, min(kMaxN, ncap));
     const int stage_bytes = kATileBytes + ncap * 128;
-    const int ring = kDynSmem - 1024 - static_cast<int>(sizeof(float)) * kXchgFloats;
     s_ntouched = nt;
     s_ncap = ncap;
-    s_stages = min(kMaxStages, ring / stage_bytes);
+    s_stages = min(kMaxStages, (kDynSmem - 1024) / stage_bytes);
   }
   tc_fence_before();
   __syncthreads();
@@ -161,53 +213,73 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ncap = s_ncap;
   const int nstages = s_stages;
   const int stage_bytes = kATileBytes + ncap * 128;
-  const int total_units = s_ntouched * m_tiles * splits;
-  float* xchg = reinterpret_cast<float*>(ring_gen + nstages * stage_bytes);
+  const int nbuf = ncap <= 128 ? 2 : 1;
+  const uint32_t acc1_off = nbuf == 2 ? 128u : 256u;
+
+  Geometry g;
+  g.m1 = (I + 127) / 128;
+  g.m2 = (H + 255) / 256;
+  g.kb1_total = H / kBK;
+  g.kb2_total = I / kBK;
+  g.splits = args.splits;
+  g.n1 = do1 ? s_ntouched * g.m1 : 0;
+  g.n2 = do2 ? s_ntouched * g.m2 * g.splits : 0;
+  g.total = g.n1 + g.n2;
+
+  // Units are handed out dynamically: the producer claims the next unit id from a
+  // global counter (zeroed by the router) and publishes it through a small queue in
+  // shared memory; the other roles read the same ids in the same order.  Claims run in
+  // increasing order, so every gate/up unit is claimed before any down unit.
+  auto next_unit = [&](int& qi, uint32_t& qph) -> int {
+    if (!mbar_wait(&qfull_bar[qi], qph, args.status, &s_abort)) return -1;
+    const int u = *reinterpret_cast<volatile int*>(&s_queue[qi]);
+    mbar_arrive(&qempty_bar[qi]);
+    if (++qi == kQueue) {
+      qi = 0;
+      qph ^= 1u;
+    }
+    return u;
+  };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (weights)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_b = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
+      int qi = 0;
+      uint32_t qph = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
-        const Unit un = decode_unit<MODE>(u, m_tiles, splits, kb_total);
+      while (ok) {
+        if (!mbar_wait(&qempty_bar[qi], qph ^ 1u, args.status, &s_abort)) break;
+        int u = atomicAdd(args.sched, 1);
+        if (u >= g.total) u = -1;
+        s_queue[qi] = u;
+        mbar_arrive(&qfull_bar[qi]);
+        if (++qi == kQueue) {
+          qi = 0;
+          qph ^= 1u;
+        }
+        if (u < 0) break;
+        const Unit un = decode(u, g);
         const int e = s_touched[un.te];
         const int page = s_page[un.te];
-        const int row0 = args.expert_off[e];
-        const int n_e = args.expert_off[e + 1] - row0;
-        const int wrow = (MODE == kGateUp) ? page * 3 * I + un.mt * 64 : page * 3 * H + 2 * H + un.mt * 128;
+        const int n_e = args.expert_off[e + 1] - args.expert_off[e];
+        const CUtensorMap* map = un.phase == 1 ? &tm_w13 : &tm_w2;
+        // rows of the two 128-row boxes
+        const int r0 = un.phase == 1 ? page * 3 * I + un.mt * 128 : page * 3 * H + 2 * H + un.mt * 256;
+        const int r1 = un.phase == 1 ? r0 + I : r0 + 128;
         for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
-          const int nlen = min(ncap, n_e - n0);
-          const int nb = (nlen + 15) & ~15;
           for (int kb = un.kb0; kb < un.kb1; ++kb) {
             if (!mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort)) {
               ok = false;
               break;
             }
-            uint8_t* sA = ring_gen + stage * stage_bytes;
-            uint8_t* sB = sA + kATileBytes;
-            mbar_arrive_expect_tx(&full_bar[stage], kATileBytes + nb * 128);
-            if (MODE == kGateUp) {
-              tma_load_2d(sA, &tm_w, &full_bar[stage], kb * kBK, wrow, pol_w);
-              tma_load_2d(sA + kATileBytes / 2, &tm_w, &full_bar[stage], kb * kBK, wrow + I, pol_w);
-            } else {
-              tma_load_2d(sA, &tm_w, &full_bar[stage], kb * kBK, wrow, pol_w);
-            }
-            int r = 0;
-            const int brow = row0 + n0;
-            for (; r + 64 <= nb; r += 64) tma_load_2d(sB + r * 128, &tm_b64, &full_bar[stage], kb * kBK, brow + r, pol_b);
-            if (r + 32 <= nb) {
-              tma_load_2d(sB + r * 128, &tm_b32, &full_bar[stage], kb * kBK, brow + r, pol_b);
-              r += 32;
-            }
-            if (r + 16 <= nb) {
-              tma_load_2d(sB + r * 128, &tm_b16, &full_bar[stage], kb * kBK, brow + r, pol_b);
-              r += 16;
-            }
+            uint8_t* sA = dyn_smem + (ring_base - raw_base) + stage * stage_bytes;
+            mbar_arrive_expect_tx(&fullA_bar[stage], kATileBytes);
+            tma_load_2d(sA, map, &fullA_bar[stage], kb * kBK, r0, pol_w);
+            tma_load_2d(sA + kBoxBytes, map, &fullA_bar[stage], kb * kBK, r1, pol_w);
             ++issued;
             if (++stage == nstages) {
               stage = 0;
@@ -222,35 +294,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int stage = 0;
-      uint32_t phase = 0, tphase = 0;
+      uint32_t phase = 0;
+      int qi = 0;
+      uint32_t qph = 0;
+      int pass = 0;
       int consumed = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
-        const Unit un = decode_unit<MODE>(u, m_tiles, splits, kb_total);
+      while (ok) {
+        const int u = next_unit(qi, qph);
+        if (u < 0) break;
+        const Unit un = decode(u, g);
         const int e = s_touched[un.te];
         const int n_e = args.expert_off[e + 1] - args.expert_off[e];
-        for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
-          const int nlen = min(ncap, n_e - n0);
-          const int nb = (nlen + 15) & ~15;
+        for (int n0 = 0; ok && n0 < n_e; n0 += ncap, ++pass) {
+          const int nb = (min(ncap, n_e - n0) + 15) & ~15;
           const uint32_t idesc = idesc_f16(kBF16, 128, nb);
-          if (!mbar_wait(&tempty_bar, tphase ^ 1u, args.status, &s_abort)) {
+          const int buf = pass % nbuf;
+          if (!mbar_wait(&tempty_bar[buf], ((pass / nbuf) & 1) ^ 1u, args.status, &s_abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * 256);
+          const uint32_t acc1 = acc0 + acc1_off;
           for (int kb = un.kb0; kb < un.kb1; ++kb) {
-            if (!mbar_wait(&full_bar[stage], phase, args.status, &s_abort)) {
+            if (!mbar_wait(&fullA_bar[stage], phase, args.status, &s_abort) ||
+                !mbar_wait(&fullB_bar[stage], phase, args.status, &s_abort)) {
               ok = false;
               break;
             }
+            // the token tile was written by cp.async (generic proxy); the MMA reads it
+            // through the async proxy
+            fence_proxy_async_smem();
             tc_fence_after();
             const uint32_t a_addr = ring_base + stage * stage_bytes;
-            const uint64_t ad = desc_kmajor_sw128(a_addr);
+            const uint64_t ad0 = desc_kmajor_sw128(a_addr);
+            const uint64_t ad1 = desc_kmajor_sw128(a_addr + kBoxBytes);
             const uint64_t bd = desc_kmajor_sw128(a_addr + kATileBytes);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
               // +32 bytes along K inside the swizzle row = +2 in the encoded start address
-              umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb > un.kb0 || kk > 0) ? 1u : 0u);
+              const uint32_t acc = (kb > un.kb0 || kk > 0) ? 1u : 0u;
+              umma_f16(acc0, ad0 + 2 * kk, bd + 2 * kk, idesc, acc);
+              umma_f16(acc1, ad1 + 2 * kk, bd + 2 * kk, idesc, acc);
             }
             umma_commit(&empty_bar[stage]);
             ++consumed;
@@ -260,70 +346,157 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (!ok) break;
-          umma_commit(&tfull_bar);
-          tphase ^= 1u;
+          umma_commit(&tfull_bar[buf]);
         }
       }
       s_consumed = consumed;
     }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ token-tile loaders
+    // Lane 0 of each loader warp does every wait and broadcasts the outcome, so a wait
+    // that gives up ends the whole warp together.
+    const int bt = threadIdx.x - 64;
+    const T* xp = reinterpret_cast<const T*>(args.xp);
+    const T* a2 = reinterpret_cast<const T*>(args.a2);
+    const unsigned full = 0xffffffffu;
+    int stage = 0;
+    uint32_t phase = 0;
+    int qi = 0;
+    uint32_t qph = 0;
+    bool ok = true;
+    while (ok) {
+      int u = 0;
+      if (lane == 0) u = next_unit(qi, qph);
+      u = __shfl_sync(full, u, 0);
+      if (u < 0) break;
+      const Unit un = decode(u, g);
+      const int e = s_touched[un.te];
+      const int row0 = args.expert_off[e];
+      const int n_e = args.expert_off[e + 1] - row0;
+      const T* src = un.phase == 1 ? xp : a2;
+      const int K = un.phase == 1 ? H : I;
+      if (un.phase == 2 && chained) {
+        // A2 rows of expert e are complete once all its gate/up units have counted in
+        int ready = 0;
+        if (lane == 0) {
+          const uint64_t t0 = global_timer_ns();
+          while (true) {
+            if (ld_acquire(args.done + e) >= g.m1) {
+              ready = 1;
+              break;
+            }
+            if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+            if (global_timer_ns() - t0 > kWaitBudgetNs) {
+              record_status(args.status, kDevTimeout);
+              s_abort = 1;
+              break;
+            }
+          }
+        }
+        ready = __shfl_sync(full, ready, 0);
+        if (!ready) break;
+      }
+      for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
+        const int nlen = min(ncap, n_e - n0);
+        const int nb = (nlen + 15) & ~15;
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+          int got = 0;
+          if (lane == 0) got = mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort) ? 1 : 0;
+          got = __shfl_sync(full, got, 0);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          const uint32_t sB = ring_base + stage * stage_bytes + kATileBytes;
+          // nb rows x 8 chunks of 16 B, written with the 128-byte swizzle (chunk ^ row%8)
+          for (int c = bt; c < nb * 8; c += kLoaderThreads) {
+            const int r = c >> 3;
+            const int q = c & 7;
+            const bool valid = r < nlen;
+            const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
+            cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid);
+          }
+          cp_async_arrive_noinc(&fullB_bar[stage]);
+          if (++stage == nstages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    cp_async_wait_all();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;          // TMEM lane quarter this warp may read
     const int row = sub * 32 + lane;   // accumulator row = TMEM lane
     const int et = threadIdx.x - 128;  // 0..127
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-    uint32_t tphase = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-      const Unit un = decode_unit<MODE>(u, m_tiles, splits, kb_total);
+    int qi = 0;
+    uint32_t qph = 0;
+    int pass = 0;
+    bool ok = true;
+    while (ok) {
+      // the leader reads the queue; the id is broadcast so all 128 threads agree
+      if (et == 0) s_epi_unit = next_unit(qi, qph);
+      named_bar_sync(1, 128);
+      const int u = s_epi_unit;
+      named_bar_sync(1, 128);
+      if (u < 0) break;
+      const Unit un = decode(u, g);
       const int e = s_touched[un.te];
       const int row0 = args.expert_off[e];
       const int n_e = args.expert_off[e + 1] - row0;
-      bool ok = true;
-      for (int n0 = 0; n0 < n_e; n0 += ncap) {
+      for (int n0 = 0; n0 < n_e; n0 += ncap, ++pass) {
         const int nlen = min(ncap, n_e - n0);
-        if (et == 0) s_epi_ok = mbar_wait(&tfull_bar, tphase, args.status, &s_abort) ? 1 : 0;
+        const int buf = pass % nbuf;
+        if (et == 0) {
+          s_epi_ok = mbar_wait(&tfull_bar[buf], (pass / nbuf) & 1, args.status, &s_abort) ? 1 : 0;
+        }
         named_bar_sync(1, 128);
         ok = s_epi_ok != 0;
         named_bar_sync(1, 128);
         if (!ok) break;
         tc_fence_after();
+        const uint32_t lane_base =
+            tmem + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(buf * 256);
         for (int c0 = 0; c0 < nlen; c0 += 16) {
-          float v[16];
-          tmem_ld16(lane_addr + static_cast<uint32_t>(c0), v);
-          if (MODE == kGateUp) {
-            if (sub >= 2) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) xchg[i * 64 + (row - 64)] = v[i];
-            }
-            named_bar_sync(1, 128);
-            if (sub < 2) {
-              T* a2 = reinterpret_cast<T*>(args.out);
-              const size_t col = static_cast<size_t>(un.mt) * 64 + row;
+          float va[16], vb[16];
+          tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
+          tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
+          if (un.phase == 1) {
+            T* out = reinterpret_cast<T*>(args.a2);
+            const int f = un.mt * 128 + row;
+            if (f < I) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                if (c0 + i < nlen) {
-                  const float up = xchg[i * 64 + row];
-                  a2[static_cast<size_t>(row0 + n0 + c0 + i) * I + col] = from_f32<T>(silu_f32(v[i]) * up);
+                const int p = row0 + n0 + c0 + i;
+                if (c0 + i < nlen && p >= 0 && p < args.Tk) {
+                  out[static_cast<size_t>(p) * I + f] = from_f32<T>(silu_f32(va[i]) * vb[i]);
                 }
               }
             }
-            named_bar_sync(1, 128);
           } else {
-            float* part = reinterpret_cast<float*>(args.out);
-            const size_t h = static_cast<size_t>(un.mt) * 128 + row;
+            const int h0 = un.mt * 256 + row;
+            const int h1 = h0 + 128;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              if (c0 + i < nlen) {
-                part[(static_cast<size_t>(un.ks) * args.Tk + row0 + n0 + c0 + i) * H + h] = v[i];
+              const int p = row0 + n0 + c0 + i;
+              if (c0 + i < nlen && p >= 0 && p < args.Tk) {
+                float* dst = args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H;
+                if (h0 < H) dst[h0] = va[i];
+                if (h1 < H) dst[h1] = vb[i];
               }
             }
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty_bar);
-        tphase ^= 1u;
+        mbar_arrive(&tempty_bar[buf]);
       }
-      if (!ok) break;
+      if (ok && un.phase == 1 && chained) {
+        // publish: this unit's A2 columns are written (release at GPU scope)
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) atomicAdd(args.done + e, 1);
+      }
     }
   }
 
@@ -331,11 +504,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (s_abort) {
-    // Unwind after a failed wait: let our own TMA fills and MMAs land before the
+    // Unwind after a failed wait: let our own weight fills and MMAs land before the
     // shared and tensor memory they target is released.
     if (threadIdx.x == 0) {
       for (int i = s_consumed; i < s_issued; ++i) {
-        mbar_wait(&full_bar[i % nstages], static_cast<uint32_t>((i / nstages) & 1), nullptr, nullptr);
+        mbar_wait(&fullA_bar[i % nstages], static_cast<uint32_t>((i / nstages) & 1), nullptr, nullptr);
       }
     }
     if (threadIdx.x == 32) {
@@ -352,9 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-static cudaError_t launch_one(const void* fn, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& a,
-                              const CUtensorMap& b64, const CUtensorMap& b32, const CUtensorMap& b16,
-                              const FfnArgs& args) {
+cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
+                            const CUtensorMap& w2, const FfnArgs& args) {
+  static std::atomic<int> seen_bf16[64], seen_f16[64];
+  const void* fn = bf16 ? reinterpret_cast<const void*>(&ffn_gemm_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&ffn_gemm_kernel<__half>);
+  cudaError_t err = ensure_dyn_smem(fn, kDynSmem, bf16 ? seen_bf16 : seen_f16, 64);
+  if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -365,33 +542,8 @@ static cudaError_t launch_one(const void* fn, int grid, cudaStream_t stream, boo
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* params[] = {const_cast<CUtensorMap*>(&a), const_cast<CUtensorMap*>(&b64), const_cast<CUtensorMap*>(&b32),
-                    const_cast<CUtensorMap*>(&b16), const_cast<FfnArgs*>(&args)};
+  void* params[] = {const_cast<CUtensorMap*>(&w13), const_cast<CUtensorMap*>(&w2), const_cast<FfnArgs*>(&args)};
   return cudaLaunchKernelExC(&cfg, fn, params);
-}
-
-template <int MODE, typename T>
-static cudaError_t launch_mode(int grid, cudaStream_t stream, bool pdl, const CUtensorMap& a, const CUtensorMap& b64,
-                               const CUtensorMap& b32, const CUtensorMap& b16, const FfnArgs& args) {
-  const void* fn = reinterpret_cast<const void*>(&ffn_gemm_kernel<MODE, T>);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
-  if (err != cudaSuccess) return err;
-  return launch_one(fn, grid, stream, pdl, a, b64, b32, b16, args);
-}
-
-cudaError_t launch_ffn_gemm(int mode, bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& a,
-                            const CUtensorMap& b64, const CUtensorMap& b32, const CUtensorMap& b16,
-                            const FfnArgs& args) {
-  if (mode == kGateUp) {
-    return bf16 ? launch_mode<kGateUp, __nv_bfloat16>(grid, stream, pdl, a, b64, b32, b16, args)
-                : launch_mode<kGateUp, __half>(grid, stream, pdl, a, b64, b32, b16, args);
-  }
-  return bf16 ? launch_mode<kDown, __nv_bfloat16>(grid, stream, pdl, a, b64, b32, b16, args)
-              : launch_mode<kDown, __half>(grid, stream, pdl, a, b64, b32, b16, args);
-}
-
-int ffn_units(int mode, int E, int H, int I, int splits) {
-  return mode == kGateUp ? E * (I / 64) : E * (H / 128) * splits;
 }
 
 }  // namespace smb

@@ -4,27 +4,46 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "layout.h"
 
 namespace smb {
 
-enum FfnMode { kGateUp = 1, kDown = 2 };
+// Raise a kernel's dynamic shared-memory limit on the current device unless an earlier
+// call already raised it at least as far (the attribute lasts for the process).  One
+// `seen` table per kernel; concurrent first calls may both set it, which is harmless.
+inline cudaError_t ensure_dyn_smem(const void* fn, int bytes, std::atomic<int>* seen, int seen_len) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 0 && dev < seen_len && seen[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess && dev >= 0 && dev < seen_len) {
+    int cur = seen[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !seen[dev].compare_exchange_weak(cur, bytes)) {
+    }
+  }
+  return err;
+}
 
 struct FfnArgs {
   const int32_t* expert_off;      // [E+1]
   const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
   int* status;                    // device status word
-  void* out;                      // kGateUp: A2 [rows, I] storage dtype; kDown: fp32 [S, Tk, H]
+  int* done;                      // [E] finished gate/up units per expert (zeroed by the router)
+  int* sched;                     // [1] next unit to hand out (zeroed by the router)
+  const void* xp;                 // [rows, H] token rows, expert-major
+  void* a2;                       // [rows, I] activations, expert-major
+  float* part;                    // [S, Tk, H] split-K partials of the down projection
   long long num_pages;            // P
   int E, H, I, Tk, splits;
+  int phase_mask;                 // 1: gate/up, 2: down, 3: both in one launch
 };
 
-cudaError_t launch_ffn_gemm(int mode, bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& a,
-                            const CUtensorMap& b64, const CUtensorMap& b32, const CUtensorMap& b16,
-                            const FfnArgs& args);
-int ffn_units(int mode, int E, int H, int I, int splits);
+cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
+                            const CUtensorMap& w2, const FfnArgs& args);
 
 struct RouteArgs {
   const void* logits;      // [T, E] or nullptr (routing given)
@@ -42,6 +61,7 @@ struct RouteArgs {
   int32_t* ws_ids;
   void* xp;
   int* status;
+  int* done;               // [E+1] per-expert counters + work counter of the FFN kernel, zeroed here
   int rows_per_cta;
 };
 

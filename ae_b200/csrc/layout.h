@@ -26,6 +26,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct WsLayout {
   size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert
   size_t status;      // int32 [8]     device status word(s)
+  size_t done;        // int32 [E+1]   finished gate/up units per expert, then the FFN work counter
   size_t perm;        // int32 [Tk]    perm[p] = flat slot f = t*k + j at position p
   size_t inv;         // int32 [Tk]    inv[f] = p
   size_t w;           // fp32  [Tk]    routing weight of flat slot f
@@ -46,6 +47,7 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   size_t o = 0;
   L.expert_off = o; o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
   L.status = o;     o = align_up(o + sizeof(int32_t) * 8, kAlign);
+  L.done = o;       o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
   L.perm = o;       o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.inv = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.w = o;          o = align_up(o + sizeof(float) * Tk, kAlign);
@@ -57,16 +59,29 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   return L;
 }
 
-// Split-K factor of the down projection: enough (expert, 128-row tile, split) units
-// for about two per SM when every expert is touched, never more splits than 64-wide
-// K blocks.
-inline int choose_splits(int E, int H, int I, int num_sms) {
-  const int tiles = E * (H / 128);
-  int s = (2 * num_sms + tiles - 1) / tiles;
-  const int kb = I / 64;
-  if (s < 1) s = 1;
-  if (s > kb) s = kb;
-  return s;
+// Split-K factor of the down projection.  The FFN kernel hands out units dynamically,
+// gate/up units first, so the run ends with a tail of about half a down unit (256 rows x
+// I/S) during which SMs fall idle one by one.  More splits shorten that tail but add fp32
+// partials that the kernel writes and the combine reads back.  Pick S in
+// [1, min(16, I/64)] minimising tail + partial traffic, at a per-SM streaming rate of
+// 45 GB/s and an HBM rate of 6.5 TB/s.
+inline int choose_splits(int E, int H, int I, int Tk, int num_sms) {
+  (void)E;
+  (void)num_sms;
+  const double per_sm = 45e9, hbm = 6.5e12;
+  const int kb2 = I / 64;
+  const int smax = kb2 < 16 ? kb2 : 16;
+  int best = 1;
+  double best_t = 1e30;
+  for (int s = 1; s <= smax; ++s) {
+    const double unit = 256.0 * ((kb2 + s - 1) / s) * 64 * 2;
+    const double t = 0.5 * unit / per_sm + 2.0 * s * static_cast<double>(Tk) * H * 4 / hbm;
+    if (t < best_t * 0.999) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace smb

@@ -34,64 +34,113 @@ __device__ __forceinline__ float logit_at(const void* base, size_t idx) {
   return to_f32<TL>(reinterpret_cast<const TL*>(base)[idx]);
 }
 
-// Top-k of one token's logits by one warp.  Lane j < k ends with (id_j, w_j).
-template <typename TL>
-__device__ __forceinline__ void route_token(const void* logits, int t, int E, int k, int renorm, int lane,
-                                            int& my_id, float& my_w) {
-  float v[kMaxExperts / 32];
+// Top-k of one token's logits by a group of G lanes (G a power of two, G * 8 >= E):
+// lane q of the group holds experts q, q+G, q+2G, ... (at most 8).  Reductions are
+// xor-shuffles inside the group, so every lane of the group ends with all k (id, w).
+// Ties go to the lower expert index.  The probabilities follow select_experts:
+// p = exp(x - max) * (1 / sum), then (renormalise) p_j / sum of the k selected p.
+template <typename TL, int G>
+__device__ __forceinline__ void route_token_group(const void* logits, int t, int E, int k, int renorm, int q,
+                                                  int (&ids)[kMaxTopK], float (&ws)[kMaxTopK]) {
+  constexpr int kPer = 8;
+  float v[kPer];
   const size_t row = static_cast<size_t>(t) * E;
   float m = -INFINITY;
 #pragma unroll
-  for (int r = 0; r < kMaxExperts / 32; ++r) {
-    const int e = lane + 32 * r;
+  for (int r = 0; r < kPer; ++r) {
+    const int e = q + G * r;
     v[r] = (e < E) ? logit_at<TL>(logits, row + e) : -INFINITY;
     m = fmaxf(m, v[r]);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+  for (int o = G / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
   float s = 0.f;
 #pragma unroll
-  for (int r = 0; r < kMaxExperts / 32; ++r) {
-    const int e = lane + 32 * r;
-    if (e < E) s += expf(v[r] - m);
+  for (int r = 0; r < kPer; ++r) {
+    if (q + G * r < E) s += expf(v[r] - m);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
   const float inv_s = 1.0f / s;
 
   unsigned taken = 0;
   float sel_sum = 0.f;
-  my_id = -1;
-  my_w = 0.f;
-  for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
-    int be = INT_MAX;
 #pragma unroll
-    for (int r = 0; r < kMaxExperts / 32; ++r) {
-      const int e = lane + 32 * r;
-      if (e < E && !((taken >> r) & 1u) && (be == INT_MAX || v[r] > bv)) {
-        bv = v[r];
-        be = e;
-      }
-    }
+  for (int j = 0; j < kMaxTopK; ++j) {
+    ids[j] = -1;
+    ws[j] = 0.f;
+    if (j < k) {
+      float bv = -INFINITY;
+      int be = INT_MAX;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(kFull, bv, o);
-      const int oe = __shfl_xor_sync(kFull, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
+      for (int r = 0; r < kPer; ++r) {
+        const int e = q + G * r;
+        if (e < E && !((taken >> r) & 1u) && (be == INT_MAX || v[r] > bv)) {
+          bv = v[r];
+          be = e;
+        }
       }
-    }
-    if (lane == (be & 31)) taken |= 1u << (be >> 5);
-    const float p = expf(bv - m) * inv_s;
-    sel_sum += p;
-    if (lane == j) {
-      my_id = be;
-      my_w = p;
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, o);
+        const int oe = __shfl_xor_sync(kFull, be, o);
+        if (ov > bv || (ov == bv && oe < be)) {
+          bv = ov;
+          be = oe;
+        }
+      }
+      if (be != INT_MAX && q == (be % G)) taken |= 1u << (be / G);
+      const float p = expf(bv - m) * inv_s;
+      sel_sum += p;
+      ids[j] = be;
+      ws[j] = p;
     }
   }
-  if (renorm && lane < k) my_w = my_w / sel_sum;
+  if (renorm) {
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) ws[j] = ws[j] / sel_sum;
+  }
+}
+
+// Route tokens [t_begin, t_end) with groups of G lanes over nthreads threads; writes
+// ids / weights of slot t*k+j through the callback.
+template <typename TL, int G, typename Sink>
+__device__ __forceinline__ void route_range(const void* logits, int t_begin, int t_end, int E, int k, int renorm,
+                                            int tid, int nthreads, Sink sink) {
+  const int q = tid & (G - 1);
+  const int groups = nthreads / G;
+  // every lane of a warp runs the same number of iterations (shuffles stay converged)
+  for (int base = t_begin; base < t_end; base += groups) {
+    const int t = base + tid / G;
+    const int tc = t < t_end ? t : t_end - 1;
+    int ids[kMaxTopK];
+    float ws[kMaxTopK];
+    route_token_group<TL, G>(logits, tc, E, k, renorm, q, ids, ws);
+    if (t < t_end) {
+#pragma unroll
+      for (int j = 0; j < kMaxTopK; ++j) {
+        if (j < k && (j % G) == q) sink(t * k + j, ids[j], ws[j]);
+      }
+    }
+  }
+}
+
+template <typename TL, typename Sink>
+__device__ __forceinline__ void route_dispatch(const void* logits, int t_begin, int t_end, int E, int k,
+                                               int renorm, int tid, int nthreads, Sink sink) {
+  if (E <= 8) {
+    route_range<TL, 1>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  } else if (E <= 16) {
+    route_range<TL, 2>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  } else if (E <= 32) {
+    route_range<TL, 4>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  } else if (E <= 64) {
+    route_range<TL, 8>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  } else if (E <= 128) {
+    route_range<TL, 16>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  } else {
+    route_range<TL, 32>(logits, t_begin, t_end, E, k, renorm, tid, nthreads, sink);
+  }
 }
 
 template <typename TL>
@@ -120,15 +169,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
 
   // 1. routing of every token (or the given routing)
   if (a.logits != nullptr) {
-    for (int t = warp; t < a.T; t += kRouteWarps) {
-      int id;
-      float w;
-      route_token<TL>(a.logits, t, E, a.k, a.renormalize, lane, id, w);
-      if (lane < a.k) {
-        s_ids[t * a.k + lane] = id;
-        s_w[t * a.k + lane] = w;
-      }
-    }
+    route_dispatch<TL>(a.logits, 0, a.T, E, a.k, a.renormalize, tid, kRouteThreads, [&](int f, int id, float w) {
+      s_ids[f] = id;
+      s_w[f] = w;
+    });
   } else {
     for (int f = tid; f < Tk; f += kRouteThreads) {
       int id = a.in_ids[f];
@@ -211,6 +255,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   // 5. outputs for this CTA's flat range
   if (blockIdx.x == 0) {
     for (int e = tid; e <= E; e += kRouteThreads) a.expert_off[e] = s_off[e];
+    if (a.done != nullptr) {
+      for (int e = tid; e <= E; e += kRouteThreads) a.done[e] = 0;
+    }
   }
   const int g0 = min(Tk, static_cast<int>(blockIdx.x) * a.rows_per_cta);
   const int g1 = min(Tk, g0 + a.rows_per_cta);
@@ -238,16 +285,15 @@ __global__ void __launch_bounds__(256) topk_kernel(const void* logits, int T, in
                                                    float* out_w, int32_t* out_ids) {
   pdl_wait_prior_grids();
   pdl_launch_dependents();
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (t >= T) return;
-  int id;
-  float w;
-  route_token<TL>(logits, t, E, k, renorm, lane, id, w);
-  if (lane < k) {
-    out_w[static_cast<size_t>(t) * k + lane] = w;
-    out_ids[static_cast<size_t>(t) * k + lane] = id;
-  }
+  // this CTA's tokens: a contiguous range sized for 256 lanes in groups of 32 (covers E <= 256)
+  const int per_cta = blockDim.x / 32;
+  const int t0 = blockIdx.x * per_cta;
+  const int t1 = min(T, t0 + per_cta);
+  if (t0 >= T) return;
+  route_dispatch<TL>(logits, t0, t1, E, k, renorm, threadIdx.x, blockDim.x, [&](int f, int id, float w) {
+    out_w[f] = w;
+    out_ids[f] = id;
+  });
 }
 
 }  // namespace
@@ -271,14 +317,16 @@ size_t route_smem_bytes(int T, int E, int k) {
 }
 
 cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStream_t stream, bool pdl) {
+  static std::atomic<int> seen[3][64];
   const void* fn = nullptr;
+  int which = 0;
   switch (a.logits == nullptr ? SMB_DTYPE_F32 : a.logits_dtype) {
-    case SMB_DTYPE_F16: fn = reinterpret_cast<const void*>(&route_kernel<__half>); break;
-    case SMB_DTYPE_BF16: fn = reinterpret_cast<const void*>(&route_kernel<__nv_bfloat16>); break;
-    default: fn = reinterpret_cast<const void*>(&route_kernel<float>); break;
+    case SMB_DTYPE_F16: fn = reinterpret_cast<const void*>(&route_kernel<__half>); which = 0; break;
+    case SMB_DTYPE_BF16: fn = reinterpret_cast<const void*>(&route_kernel<__nv_bfloat16>); which = 1; break;
+    default: fn = reinterpret_cast<const void*>(&route_kernel<float>); which = 2; break;
   }
   const size_t smem = route_smem_bytes(a.T, a.E, a.k);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t err = smem > 48 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[which], 64) : cudaSuccess;
   if (err != cudaSuccess) return err;
   int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * elem_bytes / 16);
   cudaLaunchConfig_t cfg = {};

@@ -80,8 +80,8 @@ def workspace_bytes(T: int, E: int, k: int, H: int, I: int, dtype: torch.dtype) 
     return int(n)
 
 
-def splits(E: int, H: int, I: int) -> int:
-    return _native.call("smb_moe_splits", E, H, I)
+def splits(E: int, H: int, I: int, Tk: int) -> int:
+    return _native.call("smb_moe_splits", E, H, I, Tk)
 
 
 def pool_geometry(pool: torch.Tensor, H: int):
@@ -241,10 +241,11 @@ class StagedLayer:
             return (v + A - 1) // A * A
 
         rows = up_to(Tk, 64) + 64
-        S = splits(E, H, I)
+        S = splits(E, H, I, Tk)
         o = 0
         off = {}
-        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("perm", 4 * Tk), ("inv", 4 * Tk),
+        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E + 1)), ("perm", 4 * Tk),
+                         ("inv", 4 * Tk),
                          ("w", 4 * Tk), ("ids", 4 * Tk), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
                          ("part", 4 * S * Tk * H)):
             off[name] = (o, nb)
@@ -258,6 +259,7 @@ class StagedLayer:
         return {
             "expert_off": view("expert_off", torch.int32, (E + 1,)),
             "status": view("status", torch.int32, (8,)),
+            "done": view("done", torch.int32, (E + 1,)),
             "perm": view("perm", torch.int32, (Tk,)),
             "inv": view("inv", torch.int32, (Tk,)),
             "w": view("w", torch.float32, (Tk,)),

@@ -3,17 +3,18 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2-256] [--impl reference]
 
-A step is one pass of the MoE layer (route, gate/up GEMM + SiLU*mul, down GEMM, combine)
-over one verify batch of T synthetic tokens, inputs resident in HBM.  The timed region
-is K back-to-back steps between CUDA events on the launching stream, bracketed by a
-barrier and a device synchronise, max over ranks.  Expert weights (2.8 GB for
+A step is one pass of the MoE layer (route, expert FFN = gate/up GEMM + SiLU*mul + down
+GEMM, combine) over one verify batch of T synthetic tokens, inputs resident in HBM.  The
+timed region is K back-to-back replays of a CUDA graph holding one layer call, between
+CUDA events on the launching stream, bracketed by a barrier and a device synchronise,
+max over ranks (the eager, ctypes-per-call time is reported beside it).  Expert weights (2.8 GB for
 Mixtral-8x7B) are far larger than the 126 MB L2, so consecutive steps do not reuse
 weights from L2.
 
 N > 1: every rank holds all experts and runs its own batch of T tokens (data-parallel
 replicas of the layer, weak scaling, no collective on the data path).
 
-Extra keys: roofline (dominant kernel = gate/up GEMM, HBM bound), cpu_baseline (the CPU
+Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound), cpu_baseline (the CPU
 oracle port of the reference's arithmetic on this host), e2e (FusedMoE.forward with host
 inputs copied in and the output copied out every step), clocks, gpu_launches, kernels
 (per-kernel µs from a staged pass), sweep (other verify batch sizes).
@@ -206,12 +207,30 @@ def run_reference_arm(args, cfg, rank):
 # ---------------------------------------------------------------------------- GPU arm
 
 def algorithmic(cfg, touched: int, Tk: int, splits: int):
+    """Algorithmic bytes of the FFN kernel (touched experts' weights + its token rows in +
+    fp32 partials out) and of the whole layer (weights + tokens in and out + logits), and
+    the layer's flops."""
     H, I, T, E = cfg.H, cfg.I, cfg.T, cfg.E
-    gate_up = touched * 2 * I * H * 2 + Tk * H * 2 + Tk * I * 2
-    down = touched * H * I * 2 + Tk * I * 2 + splits * Tk * H * 4
+    ffn = touched * 3 * H * I * 2 + Tk * H * 2 + splits * Tk * H * 4
     layer = touched * 3 * H * I * 2 + 2 * T * H * 2 + T * E * 2
     flops = 6 * H * I * Tk
-    return gate_up, down, layer, flops
+    return ffn, layer, flops
+
+
+def graph_of(fn, dev):
+    """Capture one call of ``fn`` into a CUDA graph (after a warm call on the capture
+    stream, so its workspace exists before capture)."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize(dev)
+    return g
 
 
 def timed_steps(fn, steps, stream):
@@ -262,11 +281,19 @@ def run_ours(args, cfg, rank, world, dev):
             step()
         torch.cuda.synchronize(dev)
 
-    # timed region
+    # eager launches (host-side ctypes call per layer), for reference
+    torch.cuda.synchronize(dev)
+    eager = timed_steps(step, args.steps, stream)
+    # the timed region replays a CUDA graph of one layer call per step (the verify step
+    # of the reference engine is graph-captured as well); launches are the same kernels
+    graph = graph_of(step, dev)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    elapsed = timed_steps(step, args.steps, stream)
+    elapsed = timed_steps(graph.replay, args.steps, stream)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -280,32 +307,29 @@ def run_ours(args, cfg, rank, world, dev):
     if not torch.isfinite(out.float()).all():
         raise RuntimeError("non-finite layer output")
 
-    # staged pass: per-kernel durations (events between the four launches)
+    # staged pass: per-kernel durations (events between the three launches of a layer call)
     L = ops.StagedLayer(cfg.T, cfg.E, cfg.k, cfg.H, cfg.I, x.dtype, dev)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.staged_steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.staged_steps)]
     for i in range(3):
         L.route(logits, x, cfg.renormalize)
-        L.gate_up(pool, pages)
-        L.down(pool, pages)
+        L.ffn(pool, pages)
         L.combine(out)
     for e in evs:
         e[0].record(stream)
         L.route(logits, x, cfg.renormalize)
         e[1].record(stream)
-        L.gate_up(pool, pages)
+        L.ffn(pool, pages)
         e[2].record(stream)
-        L.down(pool, pages)
-        e[3].record(stream)
         L.combine(out)
-        e[4].record(stream)
+        e[3].record(stream)
     torch.cuda.synchronize(dev)
-    names = ["route", "gate_up", "down", "combine"]
+    names = ["route", "ffn", "combine"]
     kern_us = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs) * 1000.0 for i, n in enumerate(names)}
     v = L.views()
     off = v["expert_off"].cpu()
     touched = int(((off[1:] - off[:-1]) > 0).sum())
-    splits = ops.splits(cfg.E, cfg.H, cfg.I)
-    gu_bytes, dn_bytes, layer_bytes, flops = algorithmic(cfg, touched, Tk, splits)
+    splits = ops.splits(cfg.E, cfg.H, cfg.I, Tk)
+    ffn_bytes, layer_bytes, flops = algorithmic(cfg, touched, Tk, splits)
 
     # end to end through the drop-in module: host inputs in, host output out, every step
     moe = FusedMoE(cfg.E, cfg.k, cfg.H, cfg.I, params_dtype=x.dtype, renormalize=cfg.renormalize, tp_size=1)
@@ -347,14 +371,17 @@ def run_ours(args, cfg, rank, world, dev):
 
             for _ in range(5):
                 s()
+            gs = graph_of(s, dev)
+            for _ in range(3):
+                gs.replay()
             torch.cuda.synchronize(dev)
             n = max(10, args.steps // 2)
-            el_s = timed_steps(s, n, stream)
+            el_s = timed_steps(gs.replay, n, stream)
             us = el_s / n * 1e6
             sweep[f"T{Ts}"] = {"us_per_layer": round(us, 2), "tokens_per_s": round(Ts / (el_s / n), 1),
                                "layer_hbm_frac": round(algorithmic(
                                    configs.MoEConfig(cfg.name, cfg.H, cfg.I, cfg.E, cfg.k, Ts, cfg.router_std),
-                                   cfg.E, Ts * cfg.k, splits)[2] / (el_s / n) / 1e9 / hbm_peak, 4)}
+                                   cfg.E, Ts * cfg.k, splits)[1] / (el_s / n) / 1e9 / hbm_peak, 4)}
 
     # CPU baseline (rank 0, N = 1)
     cpu = None
@@ -369,8 +396,8 @@ def run_ours(args, cfg, rank, world, dev):
     if rank != 0:
         return
     step_s = elapsed / args.steps
-    gu_s = kern_us["gate_up"] * 1e-6
-    achieved = gu_bytes / gu_s / 1e9
+    ffn_s = kern_us["ffn"] * 1e-6
+    achieved = ffn_bytes / ffn_s / 1e9
     traffic = load_traffic(args.config)
     line = {
         "metric": METRIC,
@@ -381,6 +408,8 @@ def run_ours(args, cfg, rank, world, dev):
         "warmup": args.warmup,
         "ms_per_step": round(step_s * 1000, 5),
         "us_per_layer": round(step_s * 1e6, 2),
+        "launch_mode": "cuda_graph (one layer call per replay)",
+        "eager_us_per_layer": round(eager / args.steps * 1e6, 2),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -391,22 +420,21 @@ def run_ours(args, cfg, rank, world, dev):
                    "experts_touched": touched, "splits": splits,
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "inputs larger than L2 (expert weights %.2f GB per step)" % (cfg.weight_bytes() / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": "gate_up (ffn_gemm_kernel<1>)", "achieved": round(achieved, 1),
-                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                     "peak_kind": peak_kind, "alg_bytes_per_launch": gu_bytes,
-                     "traffic": traffic},
+        "roofline": {"bound": "hbm", "kernel": "ffn_gemm_kernel (gate/up + down, one launch)",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                     "alg_bytes_per_launch": ffn_bytes, "traffic": traffic},
         "layer_roofline": {"alg_bytes": layer_bytes, "achieved_gbs": round(layer_bytes / step_s / 1e9, 1),
                            "frac_hbm": round(layer_bytes / step_s / 1e9 / hbm_peak, 4),
                            "tflops": round(flops / step_s / 1e12, 2),
                            "frac_tensor": round(flops / step_s / 1e12 / tc_peak, 4)},
         "kernels_us": {n: round(u, 2) for n, u in kern_us.items()},
-        "down_roofline_frac": round(dn_bytes / (kern_us["down"] * 1e-6) / 1e9 / hbm_peak, 4),
         "cpu_baseline": cpu,
         "e2e": {"value": round(world * cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size() + logits.numel() * logits.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
                 "api": "ae_b200.layers.FusedMoE.FusedMoE.forward"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 3 * args.steps,
         "clocks": clocks,
         "sweep": sweep,
     }

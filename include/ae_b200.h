@@ -77,8 +77,9 @@ SMB_API const char* smb_last_cuda_error(void);
  * current device's SM count (split-K factor), so query it on the device you run on. */
 SMB_API size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype);
 
-/* Split-K factor the down projection uses for these sizes on the current device. */
-SMB_API int smb_moe_splits(int E, int H, int I);
+/* Split-K factor the down projection uses for these sizes (Tk = T*k) on the current
+ * device. */
+SMB_API int smb_moe_splits(int E, int H, int I, int Tk);
 
 /* Router: softmax over E in fp32, top-k (ties to the lower expert index), optional
  * renormalisation; then the expert-major permutation and the gather of token rows into

@@ -44,7 +44,7 @@ def test_argument_checks_without_gpu(lib):
     assert lib.smb_moe_topk(None, 7, 1, 8, 2, 1, None, None, None) == -2
     assert lib.smb_moe_topk(None, 1, 1, 8, 9, 1, None, None, None) == -1
     assert lib.smb_moe_topk(None, 1, 0, 8, 2, 1, None, None, None) == 0  # T = 0: nothing to do
-    assert lib.smb_moe_splits(8, 100, 3584) == -1
+    assert lib.smb_moe_splits(8, 100, 3584, 64) == -1
 
 
 def test_no_host_fallback_in_product_path():
