@@ -32,9 +32,25 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     const int p = a.inv[f];
     if (p < 0 || static_cast<size_t>(p) >= Tk) continue;  // only after a failed or skipped route
     const float wj = a.w[f];
+    const float4* src = reinterpret_cast<const float4*>(a.part + static_cast<size_t>(p) * a.H) + h4;
+    const size_t split_stride = Tk * a.H / 4;  // float4 elements between splits
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < a.splits; ++sp) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(a.part + (sp * Tk + p) * a.H) + h4);
+    int sp = 0;
+    // the splits in a fixed order, four independent loads in flight
+    for (; sp + 4 <= a.splits; sp += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = __ldg(src + (sp + q) * split_stride);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s.x += v[q].x;
+        s.y += v[q].y;
+        s.z += v[q].z;
+        s.w += v[q].w;
+      }
+    }
+    for (; sp < a.splits; ++sp) {
+      const float4 v = __ldg(src + sp * split_stride);
       s.x += v.x;
       s.y += v.y;
       s.z += v.z;

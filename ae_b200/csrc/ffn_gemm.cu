@@ -58,6 +58,7 @@ constexpr int kLoaderThreads = 64;
 constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
 constexpr int kQueueReaders = 4;               // MMA thread, the two loader-warp leaders, epilogue leader
 constexpr int kDynSmem = 227 * 1024 - 3072;
+constexpr int kPrefetchBlocks = 16;            // K blocks of the first unit warmed in L2 (512 KB)
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -177,8 +178,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
 
-  // Everything above touched only this CTA's own shared and tensor memory; the routing
-  // results and the token rows come from the router launched just before.
+  // While the router (launched just before) may still run, warm L2 with the first K
+  // blocks of the gate/up unit this CTA's index would get if every expert is touched
+  // (units are claimed roughly in CTA order, and any CTA reuses what another fetched).
+  // A guess only: the prefetch is bounds-checked by the tensor map and never waited on.
+  // page_of_expert was written before the router started, so it is final here.
+  if (threadIdx.x == 0 && do1) {
+    const int m1 = (I + 127) / 128;
+    const int e = static_cast<int>(blockIdx.x) / m1;
+    if (e < E) {
+      const long long pg = args.page_of_expert[e];
+      if (pg >= 0 && pg < args.num_pages) {
+        const int r0 = static_cast<int>(pg) * 3 * I + (static_cast<int>(blockIdx.x) % m1) * 128;
+        const int kbs = min(H / kBK, kPrefetchBlocks);
+        for (int kb = 0; kb < kbs; ++kb) {
+          tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0);
+          tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0 + I);
+        }
+      }
+    }
+  }
+
+  // Everything above touched only this CTA's own shared and tensor memory (and L2
+  // hints); the routing results and the token rows come from the router.
   pdl_wait_prior_grids();
 
   if (threadIdx.x == 0) {

@@ -270,12 +270,29 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
     if (a.out_w != nullptr) a.out_w[f] = s_w[f];
     if (a.out_ids != nullptr) a.out_ids[f] = s_ids[f];
   }
+  // token rows of this CTA's flat range into xp, all threads on all rows, four
+  // independent 16-byte loads in flight per thread
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
   uint4* xdst = reinterpret_cast<uint4*>(a.xp);
-  for (int f = g0 + warp; f < g1; f += kRouteWarps) {
-    const uint4* src = xsrc + static_cast<size_t>(f / a.k) * vec_per_row;
-    uint4* dst = xdst + static_cast<size_t>(s_pos[f]) * vec_per_row;
-    for (int i = lane; i < vec_per_row; i += 32) dst[i] = __ldg(src + i);
+  const int nvec = (g1 - g0) * vec_per_row;
+  for (int base = tid; base < nvec; base += 4 * kRouteThreads) {
+    uint4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * kRouteThreads;
+      if (i < nvec) {
+        const int f = g0 + i / vec_per_row;
+        v[j] = __ldg(xsrc + static_cast<size_t>(f / a.k) * vec_per_row + (i % vec_per_row));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * kRouteThreads;
+      if (i < nvec) {
+        const int f = g0 + i / vec_per_row;
+        xdst[static_cast<size_t>(s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
+      }
+    }
   }
 }
 

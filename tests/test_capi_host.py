@@ -90,3 +90,28 @@ def test_unsupported_options_raise():
     from ae_b200.layers.FusedMoE import FusedMoE
     with pytest.raises(NotImplementedError):
         FusedMoE(4, 2, 128, 64, torch.bfloat16, tp_size=1, quant_config=object())
+
+
+def test_specmoe_shim_routes_reference_imports():
+    """`from specmoe.layers.FusedMoE import FusedMoE` (mixtral.py:54) resolves to the drop-in."""
+    import importlib
+    import sys
+    from ae_b200 import specmoe_shim
+    from ae_b200.layers import FusedMoE as ours_mod
+    from ae_b200.layers import fused_moe_kernel as ours_k
+    saved = {k: sys.modules.get(k) for k in ("specmoe", "specmoe.layers", "specmoe.layers.FusedMoE",
+                                            "specmoe.layers.fused_moe_kernel")}
+    try:
+        names = specmoe_shim.install()
+        assert names == ["specmoe.layers.FusedMoE", "specmoe.layers.fused_moe_kernel"]
+        mod = importlib.import_module("specmoe.layers.FusedMoE")
+        assert mod.FusedMoE is ours_mod.FusedMoE
+        from specmoe.layers.fused_moe_kernel import moe_align_block_size, stack_fused_moe  # noqa: F401
+        assert stack_fused_moe is ours_k.stack_fused_moe
+        assert specmoe_shim.installed()
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
