@@ -31,6 +31,7 @@ SIGNATURES = {
     "smb_moe_gate_up": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_down": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_combine": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_combine_rows": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_noalloc": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),

@@ -52,13 +52,16 @@ BY_KEY = {"c1": C1, "c2-16": C2_T16, "c2-64": C2_T64, "c2-256": C2_T256, "c3": C
           "c5": C5}
 
 
-def make_pool(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, num_pages: int | None = None):
-    """Page pool [P, 3*I*H] ~ N(0, 0.02), generated page by page on ``device``."""
-    P = num_pages or cfg.E
-    pool = torch.empty(P, cfg.page_elems, dtype=dtype, device=device)
+def make_pool(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, num_pages: int | None = None,
+              experts=None):
+    """Page pool [P, 3*I*H] ~ N(0, 0.02), generated page by page on ``device``.  Page p
+    holds expert ``experts[p]`` (default: expert p); an expert's page is the same whichever
+    pool (a rank's shard or the whole set) it is generated into."""
+    ids = list(experts) if experts is not None else list(range(num_pages or cfg.E))
+    pool = torch.empty(len(ids), cfg.page_elems, dtype=dtype, device=device)
     g = torch.Generator(device=device)
-    for p in range(P):
-        g.manual_seed(seed * 1000003 + p)
+    for p, e in enumerate(ids):
+        g.manual_seed(seed * 1000003 + e)
         pool[p].normal_(0.0, 0.02, generator=g)
     return pool
 

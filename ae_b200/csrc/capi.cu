@@ -389,6 +389,20 @@ int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, int I, con
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, int k, int H, int I, const void* ws,
+                         size_t ws_bytes, smb_stream_t stream) {
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (T == 0) return SMB_OK;
+  if (rows == nullptr || out == nullptr) return SMB_ERR_NULL;
+  if (!aligned(rows, 16) || !aligned(out, 16)) return SMB_ERR_ALIGN;
+  cudaError_t err = launch_combine_rows(rows, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
+                                        dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
+                                        pdl_enabled());
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
 int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,
                     int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H, int I,
                     int renormalize, void* out, float* topk_weights, int32_t* topk_ids, void* ws,

@@ -73,6 +73,48 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   *reinterpret_cast<uint2*>(out) = pack.u;
 }
 
+// Weighted combine of per-slot rows: out[t, h] = sum_j w[t, j] * rows[inv[t*k+j]][h], in
+// that order in fp32, rows in the storage dtype (the expert outputs of the expert-parallel
+// path returned by the all-to-all, in dispatch order).
+template <typename TO>
+__global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const void* rows_v, const int32_t* inv,
+                                                                        const float* w, void* out_v, int T, int k,
+                                                                        int H) {
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  const int t = blockIdx.y;
+  const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
+  if (h4 * 4 >= H) return;
+  const size_t Tk = static_cast<size_t>(T) * k;
+  const TO* rows = reinterpret_cast<const TO*>(rows_v);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < k; ++j) {
+    const size_t f = static_cast<size_t>(t) * k + j;
+    const int p = inv[f];
+    if (p < 0 || static_cast<size_t>(p) >= Tk) continue;
+    const float wj = w[f];
+    union {
+      uint2 u;
+      TO h[4];
+    } v;
+    v.u = __ldg(reinterpret_cast<const uint2*>(rows + static_cast<size_t>(p) * H) + h4);
+    acc.x += wj * to_f32<TO>(v.h[0]);
+    acc.y += wj * to_f32<TO>(v.h[1]);
+    acc.z += wj * to_f32<TO>(v.h[2]);
+    acc.w += wj * to_f32<TO>(v.h[3]);
+  }
+  union {
+    TO h[4];
+    uint2 u;
+  } pack;
+  pack.h[0] = from_f32<TO>(acc.x);
+  pack.h[1] = from_f32<TO>(acc.y);
+  pack.h[2] = from_f32<TO>(acc.z);
+  pack.h[3] = from_f32<TO>(acc.w);
+  *reinterpret_cast<uint2*>(reinterpret_cast<TO*>(out_v) + static_cast<size_t>(t) * H + static_cast<size_t>(h4) * 4) =
+      pack.u;
+}
+
 constexpr int kAlignThreads = 1024;
 
 __global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids, int numel, int E, int block,
@@ -142,6 +184,24 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<CombineArgs*>(&a)};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
+                                int H, bool bf16, cudaStream_t stream, bool pdl) {
+  const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_rows_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&combine_rows_kernel<__half>);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((H / 4 + kCombineThreads - 1) / kCombineThreads, T);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<void**>(&rows), const_cast<int32_t**>(&inv), const_cast<float**>(&w), &out, &T,
+                    &k, &H};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

@@ -80,6 +80,9 @@ struct CombineArgs {
 
 cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream, bool pdl);
 
+cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
+                                int H, bool bf16, cudaStream_t stream, bool pdl);
+
 cudaError_t launch_align(const int32_t* ids, int numel, int E, int block, int32_t* sorted_ids, int32_t* expert_ids,
                          int32_t* num_post_pad, int max_blocks, cudaStream_t stream);
 

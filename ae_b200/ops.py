@@ -228,6 +228,10 @@ class StagedLayer:
         _native.call("smb_moe_combine", out.data_ptr(), self.code, self.T, self.E, self.k, self.H, self.I,
                      self.ws.data_ptr(), self.nbytes, self._s())
 
+    def combine_rows(self, rows, out):
+        _native.call("smb_moe_combine_rows", rows.data_ptr(), out.data_ptr(), self.code, self.T, self.E, self.k,
+                     self.H, self.I, self.ws.data_ptr(), self.nbytes, self._s())
+
     def status(self):
         return _status(self.ws, self.T, self.E, self.k, self.H, self.I, self.code, self._s())
 

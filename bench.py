@@ -11,8 +11,9 @@ max over ranks (the eager, ctypes-per-call time is reported beside it).  Expert 
 Mixtral-8x7B) are far larger than the 126 MB L2, so consecutive steps do not reuse
 weights from L2.
 
-N > 1: every rank holds all experts and runs its own batch of T tokens (data-parallel
-replicas of the layer, weak scaling, no collective on the data path).
+N > 1: expert parallelism (ae_b200/ep.py).  Rank r holds experts [r*E/N, (r+1)*E/N) and
+its own batch of T tokens; rows are dispatched and returned with NCCL all-to-all (weak
+scaling in tokens: N*T tokens per step).
 
 Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound), cpu_baseline (the CPU
 oracle port of the reference's arithmetic on this host), e2e (FusedMoE.forward with host
@@ -441,6 +442,130 @@ def run_ours(args, cfg, rank, world, dev):
     print(json.dumps(line), flush=True)
 
 
+def run_ep(args, cfg, rank, world, dev):
+    """N > 1: expert parallelism.  Rank r holds experts [r*E/N, (r+1)*E/N) and its own T
+    verify tokens; tokens are dispatched and combined with NCCL all-to-all
+    (ae_b200/ep.py).  Weak scaling in tokens: N*T tokens per step."""
+    import torch.distributed as dist
+    from ae_b200 import configs
+    from ae_b200.ep import ExpertParallelMoE
+    from ae_b200.layers.FusedMoE import FusedMoE  # noqa: F401  (the single-GPU drop-in is the N=1 path)
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    stream = torch.cuda.current_stream(dev)
+    E_loc = cfg.E // world
+    pool = configs.make_pool(cfg, dev, seed=0, experts=range(rank * E_loc, (rank + 1) * E_loc))
+    x, logits = configs.make_inputs(cfg, dev, seed=rank)
+    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool)
+
+    def step():
+        return moe(x, logits)
+
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    t_soak = time.time()
+    soak_end = t_soak + args.soak
+    while time.time() < soak_end:
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    elapsed = timed_steps(step, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    t_end = time.time()
+    el = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    dist.all_reduce(el, op=dist.ReduceOp.MAX)
+    elapsed = float(el.item())
+    clocks = sampler.summary(t_soak, t_end)
+    sampler.stop()
+
+    # local expert FFN of one step, timed alone (dominant kernel of a rank)
+    rows, counts, state = moe.backend.route(x, logits)
+    send, recv, recv_counts = moe.split_sizes(counts)
+    N = sum(recv)
+    recv_rows = torch.empty(N, cfg.H, dtype=x.dtype, device=dev)
+    dist.all_to_all_single(recv_rows, rows.contiguous(), recv, send)
+    local_ids = torch.repeat_interleave(torch.arange(E_loc, dtype=torch.int32, device=dev).repeat(world),
+                                        recv_counts.to(torch.int64), output_size=N)
+    for _ in range(3):
+        moe.backend.experts(recv_rows, local_ids, pool, moe.pages, E_loc)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    ev0.record(stream)
+    for _ in range(reps):
+        moe.backend.experts(recv_rows, local_ids, pool, moe.pages, E_loc)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    expert_s = ev0.elapsed_time(ev1) / reps / 1000.0
+    touched = int((recv_counts.view(world, E_loc).sum(0) > 0).sum())
+    ffn_bytes = touched * 3 * cfg.H * cfg.I * 2 + N * cfg.H * 2 * 3  # weights + layer rows in/out
+    ach = torch.tensor([ffn_bytes / expert_s / 1e9], device=dev, dtype=torch.float64)
+    dist.all_reduce(ach, op=dist.ReduceOp.MIN)
+
+    # e2e through the public EP layer with host inputs and outputs
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    dx = torch.empty_like(x)
+    dl = torch.empty_like(logits)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        hout.copy_(moe(dx, dl), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e2e_el = timed_steps(e2e_step, args.steps, stream)
+    t = torch.tensor([e2e_el], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_el = float(t.item())
+    if rank != 0:
+        return
+    step_s = elapsed / args.steps
+    achieved = float(ach.item())
+    line = {
+        "metric": METRIC,
+        "value": round(world * cfg.T * args.steps / elapsed, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1000, 5),
+        "us_per_layer": round(step_s * 1e6, 2),
+        "launch_mode": "eager (one host synchronisation per layer call for the all-to-all split sizes)",
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: expert weights N(0,0.02) bf16, tokens N(0,1), router logits x@Wr^T "
+                f"(Wr std {cfg.router_std:.4g})",
+        "config": {"workload": cfg.name + f" expert-parallel over {world} GPUs, {cfg.T} tokens per GPU",
+                   "T_per_gpu": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
+                   "experts_per_gpu": E_loc, "parallelism": f"ep{world}",
+                   "l2": "inputs larger than L2 (expert weights %.2f GB per GPU per step)"
+                         % (cfg.weight_bytes(E_loc) / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "ffn_gemm_kernel on the received rows (slowest rank)",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None},
+        "cpu_baseline": None,
+        "e2e": {"value": round(world * cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
+                "h2d_bytes_per_step": world * (x.numel() * x.element_size() + logits.numel() * logits.element_size()),
+                "d2h_bytes_per_step": world * x.numel() * x.element_size(),
+                "api": "ae_b200.ep.ExpertParallelMoE.forward"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -477,7 +602,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         dist.barrier()
     try:
-        run_ours(args, cfg, rank, world, dev)
+        if world > 1:
+            run_ep(args, cfg, rank, world, dev)
+        else:
+            run_ours(args, cfg, rank, world, dev)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -119,6 +119,15 @@ SMB_API int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* pag
 SMB_API int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
                     smb_stream_t stream);
 
+/* Routing-weighted combine of per-slot rows: out[t] = sum_j w[t,j] * rows[p(t,j)], where
+ * rows [T*k, H] (storage dtype) are in the expert-major order of the smb_moe_route /
+ * smb_moe_permute call that used `ws` (its routing weights and positions are read from
+ * `ws`).  The expert-parallel path combines the expert outputs returned by the
+ * all-to-all with it; replaces the routed-weight multiply and torch.sum over top-k
+ * (fused_moe_kernel.py:197-201, 344-349) on the token's home rank. */
+SMB_API int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, int k, int H, int I,
+                                 const void* ws, size_t ws_bytes, smb_stream_t stream);
+
 /* Whole layer: route + ffn + combine (FusedMoE.forward, FusedMoE.py:508-532, without
  * the tensor-parallel all-reduce).  out may alias x (the reference writes in place). */
 SMB_API int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,
