@@ -176,11 +176,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   } else {
     for (int f = tid; f < Tk; f += kRouteThreads) {
       int id = a.in_ids[f];
-      if (id < 0 || id >= E) {
+      if (id != -1 && (id < 0 || id >= E)) {
         s_bad = 1;
         id = 0;
       }
-      s_ids[f] = id;
+      s_ids[f] = id;  // -1: the slot has no expert (padding of the expert-parallel exchange)
       s_w[f] = a.in_w[f];
     }
   }
@@ -192,7 +192,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   const int seg = (Tk + kRouteWarps - 1) / kRouteWarps;
   const int f0 = min(Tk, warp * seg);
   const int f1 = min(Tk, f0 + seg);
-  for (int f = f0 + lane; f < f1; f += 32) atomicAdd(&s_cnt[warp * E + s_ids[f]], 1);
+  for (int f = f0 + lane; f < f1; f += 32) {
+    if (s_ids[f] >= 0) atomicAdd(&s_cnt[warp * E + s_ids[f]], 1);
+  }
   __syncthreads();
 
   // 3. scan: per expert over warps, then over experts
@@ -239,8 +241,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   // 4. positions, in ascending flat order inside each expert
   for (int base = f0; base < f1; base += 32) {
     const int f = base + lane;
-    const bool act = f < f1;
-    const int e = act ? s_ids[f] : E + lane;  // distinct keys for idle lanes
+    const bool act = f < f1 && s_ids[f] >= 0;
+    const int e = act ? s_ids[f] : E + lane;  // distinct keys for idle lanes and empty slots
+    if (f < f1 && !act) s_pos[f] = -1;
     const unsigned peers = __match_any_sync(kFull, e);
     const int rank = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   const int g1 = min(Tk, g0 + a.rows_per_cta);
   for (int f = g0 + tid; f < g1; f += kRouteThreads) {
     const int p = s_pos[f];
-    a.perm[p] = f;
+    if (p >= 0) a.perm[p] = f;
     a.inv[f] = p;
     a.ws_w[f] = s_w[f];
     a.ws_ids[f] = s_ids[f];
@@ -282,7 +285,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        v[j] = __ldg(xsrc + static_cast<size_t>(f / a.k) * vec_per_row + (i % vec_per_row));
+        if (s_pos[f] >= 0) v[j] = __ldg(xsrc + static_cast<size_t>(f / a.k) * vec_per_row + (i % vec_per_row));
       }
     }
 #pragma unroll
@@ -290,7 +293,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        xdst[static_cast<size_t>(s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
+        if (s_pos[f] >= 0) xdst[static_cast<size_t>(s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
       }
     }
   }

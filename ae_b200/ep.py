@@ -10,14 +10,14 @@ used (``specmoe/utils/server_args.py:148,202``).  Here rank r owns experts
 1. route the local tokens (softmax / top-k over all E experts).  The permuted rows are
    expert-major, and experts are contiguous per rank, so they are already grouped by
    destination rank;
-2. all-to-all of the per-expert counts (E/G per destination), then one copy of the split
-   sizes to the host (the only synchronisation of a layer call);
-3. all-to-all of the token rows;
-4. the local experts on the received rows: the same kernels as the single-GPU layer, as a
-   routed problem with k = 1 (each received row has one local expert, weight 1), so each
-   row's expert output comes back in received order;
-5. the reverse all-to-all of those rows;
-6. the routing-weighted combine on the token's home rank.
+2. all-to-all of the per-expert counts and of the token rows, each (source, destination)
+   pair with a fixed capacity of max_tokens * k rows (the worst case), so the split sizes
+   never have to reach the host;
+3. the local experts on the received rows: the same kernels as the single-GPU layer, as a
+   routed problem with k = 1 (each received row has one local expert and weight 1; the
+   unused capacity rows carry expert -1 and are skipped);
+4. the reverse all-to-all of the expert outputs;
+5. the routing-weighted combine on the token's home rank.
 
 One process per GPU; the compute steps go through a backend object, so the exchange logic
 runs the same with the CUDA library (``CudaBackend``) or with any other implementation of
@@ -76,10 +76,17 @@ class CudaBackend:
 
 
 class ExpertParallelMoE:
-    """MoE layer over G ranks, E/G experts each (``pool`` holds this rank's pages)."""
+    """MoE layer over G ranks, E/G experts each (``pool`` holds this rank's pages).
+
+    The exchange uses fixed-capacity all-to-alls: every (source, destination) pair
+    reserves ``max_tokens * top_k`` rows, the worst case, so no count ever has to reach
+    the host and nothing can overflow; the unused rows of a pair carry expert id -1 and
+    are skipped by the kernels.  A layer call is therefore free of host synchronisation
+    and can be captured in a CUDA graph.
+    """
 
     def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
-                 pool: torch.Tensor, group=None, backend=None, renormalize: bool = True):
+                 pool: torch.Tensor, max_tokens: int, group=None, backend=None, renormalize: bool = True):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -91,34 +98,55 @@ class ExpertParallelMoE:
         if pool.shape[0] < self.E_loc or pool.shape[1] != 3 * intermediate_size * hidden_size:
             raise ValueError("pool must hold this rank's E/G expert pages [E/G, 3*I*H]")
         self.pool = pool
+        self.device = pool.device
         self.pages = torch.arange(self.E_loc, dtype=torch.int64, device=pool.device)
+        self.max_tokens = int(max_tokens)
+        self.C = self.max_tokens * top_k  # rows reserved per (source, destination) pair
         self.backend = backend or CudaBackend(num_experts, top_k, hidden_size, intermediate_size, pool.dtype,
                                               pool.device, renormalize)
+        self._slot = torch.arange(self.C, device=pool.device)
 
-    def split_sizes(self, counts: torch.Tensor):
-        """All-to-all of per-expert counts; returns (send_splits, recv_splits, recv_counts)
-        with the split lists on the host."""
-        recv_counts = torch.empty(self.G * self.E_loc, dtype=torch.int32, device=counts.device)
-        dist.all_to_all_single(recv_counts, counts.contiguous(), group=self.group)
-        both = torch.cat([counts, recv_counts]).cpu()
-        send = both[: self.E].view(self.G, self.E_loc).sum(1).tolist()
-        recv = both[self.E:].view(self.G, self.E_loc).sum(1).tolist()
-        return [int(s) for s in send], [int(r) for r in recv], recv_counts
-
-    def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor, events=None) -> torch.Tensor:
+        """``events``: optional pair of CUDA events recorded around the local expert FFN."""
         T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of this layer")
+        G, E_loc, C, H = self.G, self.E_loc, self.C, self.H
+        Tk = T * self.k
         rows, counts, state = self.backend.route(x, router_logits)
-        send, recv, recv_counts = self.split_sizes(counts)
-        N = sum(recv)
-        recv_rows = torch.empty(N, self.H, dtype=rows.dtype, device=rows.device)
-        dist.all_to_all_single(recv_rows, rows.contiguous(), recv, send, group=self.group)
-        # local expert of each received row: per source, E/G runs of recv_counts rows
-        local_ids = torch.repeat_interleave(
-            torch.arange(self.E_loc, dtype=torch.int32, device=rows.device).repeat(self.G),
-            recv_counts.to(torch.int64), output_size=N)
-        y = self.backend.experts(recv_rows, local_ids, self.pool, self.pages, self.E_loc)
-        back = torch.empty(T * self.k, self.H, dtype=rows.dtype, device=rows.device)
-        dist.all_to_all_single(back, y.contiguous(), send, recv, group=self.group)
-        return self.backend.combine(back, state, T)
+        # rows are expert-major, hence destination-major: destination d owns rows
+        # [off[d], off[d] + n[d])
+        n_dst = counts.view(G, E_loc).sum(1)
+        end_dst = torch.cumsum(n_dst, 0)
+        off_dst = end_dst - n_dst
+        if Tk > 0:
+            idx = (off_dst.unsqueeze(1) + self._slot.unsqueeze(0)).clamp_(max=Tk - 1).reshape(-1)
+            send = rows.index_select(0, idx)
+        else:
+            send = torch.zeros(G * C, H, dtype=x.dtype, device=x.device)
+        recv_counts = torch.empty(G * E_loc, dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(recv_counts, counts.to(torch.int32).contiguous(), group=self.group)
+        recv = torch.empty(G * C, H, dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(recv, send, group=self.group)
+        # local expert of received row i of source s: the run of recv_counts[s] holding
+        # i, or -1 past the rows that source actually sent
+        cum = torch.cumsum(recv_counts.view(G, E_loc).to(torch.int64), 1)
+        slots = self._slot.unsqueeze(0).expand(G, C).contiguous()
+        ids = torch.searchsorted(cum, slots, right=True)
+        ids = torch.where(slots < cum[:, -1:], ids, torch.full_like(ids, -1)).to(torch.int32).reshape(-1)
+        if events is not None:
+            events[0].record()
+        y = self.backend.experts(recv, ids, self.pool, self.pages, E_loc)
+        if events is not None:
+            events[1].record()
+        back = torch.empty(G * C, H, dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(back, y.contiguous(), group=self.group)
+        if Tk == 0:
+            return self.backend.combine(back[:0], state, T)
+        # back row of permuted position p: destination d holding p, slot p - off[d]
+        pos = torch.arange(Tk, device=x.device)
+        d = torch.searchsorted(end_dst, pos, right=True)
+        back_rows = back.index_select(0, d * C + pos - off_dst[d])
+        return self.backend.combine(back_rows, state, T)
 
     __call__ = forward

@@ -11,9 +11,9 @@ max over ranks (the eager, ctypes-per-call time is reported beside it).  Expert 
 Mixtral-8x7B) are far larger than the 126 MB L2, so consecutive steps do not reuse
 weights from L2.
 
-N > 1: expert parallelism (ae_b200/ep.py).  Rank r holds experts [r*E/N, (r+1)*E/N) and
-its own batch of T tokens; rows are dispatched and returned with NCCL all-to-all (weak
-scaling in tokens: N*T tokens per step).
+N > 1: expert parallelism (ae_b200/ep.py), strong scaling: the same verify batch of T
+tokens per step, T/N on each rank; rank r holds experts [r*E/N, (r+1)*E/N); rows are
+dispatched and returned with NCCL all-to-all.
 
 Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound), cpu_baseline (the CPU
 oracle port of the reference's arithmetic on this host), e2e (FusedMoE.forward with host
@@ -443,20 +443,23 @@ def run_ours(args, cfg, rank, world, dev):
 
 
 def run_ep(args, cfg, rank, world, dev):
-    """N > 1: expert parallelism.  Rank r holds experts [r*E/N, (r+1)*E/N) and its own T
-    verify tokens; tokens are dispatched and combined with NCCL all-to-all
-    (ae_b200/ep.py).  Weak scaling in tokens: N*T tokens per step."""
+    """N > 1: expert parallelism, strong scaling.  One verify batch of T tokens per step is
+    spread over the N ranks (T/N each); rank r holds experts [r*E/N, (r+1)*E/N); rows are
+    dispatched and returned with fixed-capacity NCCL all-to-alls (ae_b200/ep.py), with no
+    host synchronisation, so the step is replayed from a CUDA graph."""
     import torch.distributed as dist
     from ae_b200 import configs
     from ae_b200.ep import ExpertParallelMoE
-    from ae_b200.layers.FusedMoE import FusedMoE  # noqa: F401  (the single-GPU drop-in is the N=1 path)
 
     hbm_peak, tc_peak, peak_kind = peaks()
     stream = torch.cuda.current_stream(dev)
+    if cfg.T % world or cfg.E % world:
+        raise SystemExit(f"{cfg.name}: T={cfg.T} and E={cfg.E} must divide by {world} GPUs")
     E_loc = cfg.E // world
+    T_r = cfg.T // world
     pool = configs.make_pool(cfg, dev, seed=0, experts=range(rank * E_loc, (rank + 1) * E_loc))
-    x, logits = configs.make_inputs(cfg, dev, seed=rank)
-    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool)
+    x, logits = configs.make_inputs(cfg, dev, seed=rank, T=T_r)
+    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r)
 
     def step():
         return moe(x, logits)
@@ -466,48 +469,54 @@ def run_ep(args, cfg, rank, world, dev):
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize(dev)
+    eager = timed_steps(step, args.steps, stream)
+    mode = "cuda_graph (one expert-parallel layer call per replay, NCCL inside the graph)"
+    try:
+        graph = graph_of(step, dev)
+        run = graph.replay
+        for _ in range(3):
+            run()
+    except Exception as exc:  # capture unsupported here: time the eager calls instead
+        mode = f"eager (graph capture failed: {type(exc).__name__})"
+        run = step
+    torch.cuda.synchronize(dev)
     t_soak = time.time()
     soak_end = t_soak + args.soak
     while time.time() < soak_end:
-        for _ in range(10):
-            step()
+        for _ in range(20):
+            run()
         torch.cuda.synchronize(dev)
     dist.barrier()
     torch.cuda.synchronize(dev)
-    elapsed = timed_steps(step, args.steps, stream)
+    elapsed = timed_steps(run, args.steps, stream)
     torch.cuda.synchronize(dev)
     dist.barrier()
     t_end = time.time()
-    el = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+    el = torch.tensor([elapsed, eager], device=dev, dtype=torch.float64)
     dist.all_reduce(el, op=dist.ReduceOp.MAX)
-    elapsed = float(el.item())
+    elapsed, eager = float(el[0].item()), float(el[1].item())
     clocks = sampler.summary(t_soak, t_end)
     sampler.stop()
 
-    # local expert FFN of one step, timed alone (dominant kernel of a rank)
-    rows, counts, state = moe.backend.route(x, logits)
-    send, recv, recv_counts = moe.split_sizes(counts)
-    N = sum(recv)
-    recv_rows = torch.empty(N, cfg.H, dtype=x.dtype, device=dev)
-    dist.all_to_all_single(recv_rows, rows.contiguous(), recv, send)
-    local_ids = torch.repeat_interleave(torch.arange(E_loc, dtype=torch.int32, device=dev).repeat(world),
-                                        recv_counts.to(torch.int64), output_size=N)
-    for _ in range(3):
-        moe.backend.experts(recv_rows, local_ids, pool, moe.pages, E_loc)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the local expert FFN of a step, timed alone (the dominant kernel of a rank)
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     reps = 10
-    ev0.record(stream)
+    t_exp = 0.0
     for _ in range(reps):
-        moe.backend.experts(recv_rows, local_ids, pool, moe.pages, E_loc)
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    expert_s = ev0.elapsed_time(ev1) / reps / 1000.0
-    touched = int((recv_counts.view(world, E_loc).sum(0) > 0).sum())
-    ffn_bytes = touched * 3 * cfg.H * cfg.I * 2 + N * cfg.H * 2 * 3  # weights + layer rows in/out
-    ach = torch.tensor([ffn_bytes / expert_s / 1e9], device=dev, dtype=torch.float64)
+        moe(x, logits, events=ev)
+        torch.cuda.synchronize(dev)
+        t_exp += ev[0].elapsed_time(ev[1]) / 1000.0
+    t_exp /= reps
+    rows, counts, state = moe.backend.route(x, logits)
+    rc = torch.empty(world * E_loc, dtype=torch.int32, device=dev)
+    dist.all_to_all_single(rc, counts.contiguous())
+    n_recv = int(rc.sum().item())
+    touched = int((rc.view(world, E_loc).sum(0) > 0).sum().item())
+    ffn_bytes = touched * 3 * cfg.H * cfg.I * 2 + n_recv * cfg.H * 2 * 2
+    ach = torch.tensor([ffn_bytes / t_exp / 1e9], device=dev, dtype=torch.float64)
     dist.all_reduce(ach, op=dist.ReduceOp.MIN)
 
-    # e2e through the public EP layer with host inputs and outputs
+    # e2e through the public EP layer with host inputs and outputs, every step
     hx = x.cpu().pin_memory()
     hl = logits.cpu().pin_memory()
     hout = torch.empty_like(hx).pin_memory()
@@ -533,34 +542,36 @@ def run_ep(args, cfg, rank, world, dev):
     achieved = float(ach.item())
     line = {
         "metric": METRIC,
-        "value": round(world * cfg.T * args.steps / elapsed, 2),
+        "value": round(cfg.T * args.steps / elapsed, 2),
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(step_s * 1000, 5),
         "us_per_layer": round(step_s * 1e6, 2),
-        "launch_mode": "eager (one host synchronisation per layer call for the all-to-all split sizes)",
+        "launch_mode": mode,
+        "eager_us_per_layer": round(eager / args.steps * 1e6, 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: expert weights N(0,0.02) bf16, tokens N(0,1), router logits x@Wr^T "
                 f"(Wr std {cfg.router_std:.4g})",
-        "config": {"workload": cfg.name + f" expert-parallel over {world} GPUs, {cfg.T} tokens per GPU",
-                   "T_per_gpu": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
+        "config": {"workload": cfg.name + f", expert-parallel over {world} GPUs ({T_r} tokens and {E_loc} "
+                                          "experts per GPU)",
+                   "T": cfg.T, "T_per_gpu": T_r, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
                    "experts_per_gpu": E_loc, "parallelism": f"ep{world}",
                    "l2": "inputs larger than L2 (expert weights %.2f GB per GPU per step)"
                          % (cfg.weight_bytes(E_loc) / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": "ffn_gemm_kernel on the received rows (slowest rank)",
+        "roofline": {"bound": "hbm", "kernel": "local expert FFN (permute + ffn_gemm_kernel + combine), slowest rank",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None},
         "cpu_baseline": None,
-        "e2e": {"value": round(world * cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
+        "e2e": {"value": round(cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
                 "h2d_bytes_per_step": world * (x.numel() * x.element_size() + logits.numel() * logits.element_size()),
                 "d2h_bytes_per_step": world * x.numel() * x.element_size(),
                 "api": "ae_b200.ep.ExpertParallelMoE.forward"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 5 * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

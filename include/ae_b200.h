@@ -96,7 +96,9 @@ SMB_API int smb_moe_topk(const void* router_logits, int logits_dtype, int T, int
                  float* topk_weights, int32_t* topk_ids, smb_stream_t stream);
 
 /* Permutation + gather from a routing computed elsewhere (stack_fused_moe's
- * topk_weights / topk_ids arguments, fused_moe_kernel.py:257-259). */
+ * topk_weights / topk_ids arguments, fused_moe_kernel.py:257-259).  An id of -1 marks a
+ * slot with no expert: it is left out of the permutation and contributes nothing to the
+ * output (the padding rows of the expert-parallel exchange use it). */
 SMB_API int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, const void* x, int dtype, int T, int E,
                     int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
 

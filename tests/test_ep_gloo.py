@@ -33,6 +33,8 @@ class OracleBackend:
     def experts(self, rows, local_ids, pool, pages, num_local):
         out = torch.zeros_like(rows)
         for i in range(rows.shape[0]):
+            if int(local_ids[i]) < 0:  # padding row of the fixed-capacity exchange
+                continue
             w1, w3, w2 = mo.page_views(pool[int(pages[int(local_ids[i])])], self.H, self.I)
             a = torch.nn.functional.silu(w1 @ rows[i]) * (w3 @ rows[i])
             out[i] = w2 @ a
@@ -72,7 +74,7 @@ def _worker(rank, world, port, tokens, E, k, H, I, q):
         logits = torch.randn(T, E, generator=gx) * 2
         if T > 0 and rank == 0:
             logits[:, E - 1] -= 100.0  # last expert never chosen by rank 0's tokens
-        moe = ExpertParallelMoE(E, k, H, I, pool, backend=OracleBackend(E, k, H, I))
+        moe = ExpertParallelMoE(E, k, H, I, pool, max_tokens=max(tokens), backend=OracleBackend(E, k, H, I))
         out = moe(x, logits)
         if T > 0:
             w, ids = mo.select_experts(logits, k, True)

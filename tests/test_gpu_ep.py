@@ -43,7 +43,7 @@ def _worker(rank, world, port, q):
         gx = torch.Generator().manual_seed(50 + rank)
         x = torch.randn(T, H, generator=gx).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=gx).to(torch.bfloat16)
-        moe = ExpertParallelMoE(E, k, H, I, pool)
+        moe = ExpertParallelMoE(E, k, H, I, pool, max_tokens=40)
         out = moe(x.to(dev), logits.to(dev))
         out2 = moe(x.to(dev), logits.to(dev))
         torch.cuda.synchronize()
