@@ -32,6 +32,9 @@ SIGNATURES = {
     "smb_moe_down": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_combine": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_combine_rows": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_ep_dispatch": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
+    "smb_moe_ep_experts": (_I, [_P, _I, _I, _P, _L, _P, _I, _I, _I, _I, _P, _P, _S, _P]),
+    "smb_moe_ep_combine": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_noalloc": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),

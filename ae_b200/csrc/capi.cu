@@ -195,9 +195,15 @@ int route_grid(int Tk, int sms) {
   return g;
 }
 
+struct EpLayout {
+  void* send = nullptr;        // dispatch: write rows into [G][C+1][H]
+  const void* recv = nullptr;  // experts: tokens are the payload rows of [G][C+1][H]
+  int G = 0, C = 0, Eloc = 1;
+};
+
 int do_route(const void* logits, int logits_dtype, const float* in_w, const int32_t* in_ids, const void* x,
              int dtype, int T, int E, int k, int H, int I, int renorm, float* out_w, int32_t* out_ids, void* ws,
-             size_t ws_bytes, cudaStream_t stream) {
+             size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout()) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
@@ -206,7 +212,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
     return SMB_ERR_DTYPE;
   if (T == 0) return SMB_OK;
   if (x == nullptr) return SMB_ERR_NULL;
-  if (logits == nullptr && (in_w == nullptr || in_ids == nullptr)) return SMB_ERR_NULL;
+  if (logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr)) return SMB_ERR_NULL;
   if (!aligned(x, 16)) return SMB_ERR_ALIGN;
   DeviceInfo di;
   rc = device_info(&di);
@@ -233,6 +239,11 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.xp = at<void>(ws, L.xp);
   a.status = at<int>(ws, L.status);
   a.done = at<int>(ws, L.done);
+  a.ep_send = ep.send;
+  a.ep_recv = ep.recv;
+  a.ep_G = ep.G;
+  a.ep_C = ep.C;
+  a.ep_Eloc = ep.Eloc;
   const int Tk = T * k;
   const int grid = route_grid(Tk, di.sms);
   a.rows_per_cta = (Tk + grid - 1) / grid;
@@ -400,6 +411,58 @@ int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, i
   cudaError_t err = launch_combine_rows(rows, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
                                         dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
                                         pdl_enabled());
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_ep_dispatch(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
+                        int H, int I, int renormalize, int G, int C, void* send, float* topk_weights,
+                        int32_t* topk_ids, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (G < 1 || E % G != 0 || C < T * k || (E / G) * 4 > H * 2) return SMB_ERR_SHAPE;
+  if (send == nullptr || (router_logits == nullptr && T > 0)) return SMB_ERR_NULL;
+  if (!aligned(send, 16)) return SMB_ERR_ALIGN;
+  EpLayout ep;
+  ep.send = send;
+  ep.G = G;
+  ep.C = C;
+  ep.Eloc = E / G;
+  return do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize, topk_weights,
+                  topk_ids, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream), ep);
+}
+
+int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t num_pages,
+                       const int64_t* page_of_expert, int dtype, int E_loc, int H, int I, void* out_rows, void* ws,
+                       size_t ws_bytes, smb_stream_t stream) {
+  if (G < 1 || C < 1 || E_loc < 1 || E_loc * 4 > H * 2) return SMB_ERR_SHAPE;
+  if (recv == nullptr || out_rows == nullptr) return SMB_ERR_NULL;
+  if (!aligned(recv, 16) || !aligned(out_rows, 16)) return SMB_ERR_ALIGN;
+  const int T = G * C;  // payload rows, one slot each (k = 1)
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  EpLayout ep;
+  ep.recv = recv;
+  ep.G = G;
+  ep.C = C;
+  ep.Eloc = E_loc;
+  int rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
+                    ws_bytes, s, ep);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out_rows, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s);
+}
+
+int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int k, int H, int I, int G, int C,
+                       const void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (G < 1 || E % G != 0 || C < T * k) return SMB_ERR_SHAPE;
+  WsLayout L;
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (T == 0) return SMB_OK;
+  if (back == nullptr || out == nullptr) return SMB_ERR_NULL;
+  if (!aligned(back, 16) || !aligned(out, 16)) return SMB_ERR_ALIGN;
+  cudaError_t err = launch_combine_rows(back, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
+                                        dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
+                                        pdl_enabled(), at<const int32_t>(ws, L.ids),
+                                        at<const int32_t>(ws, L.expert_off), C, E / G);
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 

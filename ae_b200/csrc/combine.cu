@@ -79,7 +79,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
 template <typename TO>
 __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const void* rows_v, const int32_t* inv,
                                                                         const float* w, void* out_v, int T, int k,
-                                                                        int H) {
+                                                                        int H, const int32_t* ids,
+                                                                        const int32_t* expert_off, int ep_C,
+                                                                        int ep_Eloc) {
   pdl_wait_prior_grids();
   pdl_launch_dependents();
   const int t = blockIdx.y;
@@ -93,11 +95,17 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
     const int p = inv[f];
     if (p < 0 || static_cast<size_t>(p) >= Tk) continue;
     const float wj = w[f];
+    size_t row = static_cast<size_t>(p);
+    if (ep_C > 0) {
+      // returned expert outputs: chunk of the destination rank, slot within it
+      const int d = ids[f] / ep_Eloc;
+      row = static_cast<size_t>(d) * ep_C + (p - expert_off[d * ep_Eloc]);
+    }
     union {
       uint2 u;
       TO h[4];
     } v;
-    v.u = __ldg(reinterpret_cast<const uint2*>(rows + static_cast<size_t>(p) * H) + h4);
+    v.u = __ldg(reinterpret_cast<const uint2*>(rows + row * H) + h4);
     acc.x += wj * to_f32<TO>(v.h[0]);
     acc.y += wj * to_f32<TO>(v.h[1]);
     acc.z += wj * to_f32<TO>(v.h[2]);
@@ -188,7 +196,8 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 }
 
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
-                                int H, bool bf16, cudaStream_t stream, bool pdl) {
+                                int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids,
+                                const int32_t* expert_off, int ep_C, int ep_Eloc) {
   const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_rows_kernel<__nv_bfloat16>)
                         : reinterpret_cast<const void*>(&combine_rows_kernel<__half>);
   cudaLaunchConfig_t cfg = {};
@@ -201,7 +210,7 @@ cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<void**>(&rows), const_cast<int32_t**>(&inv), const_cast<float**>(&w), &out, &T,
-                    &k, &H};
+                    &k, &H, const_cast<int32_t**>(&ids), const_cast<int32_t**>(&expert_off), &ep_C, &ep_Eloc};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

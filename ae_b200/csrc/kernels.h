@@ -63,6 +63,11 @@ struct RouteArgs {
   int* status;
   int* done;               // [E+1] per-expert counters + work counter of the FFN kernel, zeroed here
   int rows_per_cta;
+  // expert-parallel exchange layout: G chunks of (1 header row + C payload rows) x H; a
+  // header row holds the chunk's per-local-expert counts as int32 in its first bytes
+  void* ep_send;           // dispatch: gather rows here (dst-major, capacity C) instead of xp
+  const void* ep_recv;     // receive: tokens are the payload rows, ids come from the headers
+  int ep_G, ep_C, ep_Eloc;
 };
 
 cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int k, int renorm, float* out_w,
@@ -80,8 +85,11 @@ struct CombineArgs {
 
 cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream, bool pdl);
 
+// ep_C > 0: rows are the returned expert outputs in the exchange layout [G][C][H];
+// slot f reads row (ids[f] / ep_Eloc) * ep_C + inv[f] - expert_off[(ids[f] / ep_Eloc) * ep_Eloc]
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
-                                int H, bool bf16, cudaStream_t stream, bool pdl);
+                                int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids = nullptr,
+                                const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1);
 
 cudaError_t launch_align(const int32_t* ids, int numel, int E, int block, int32_t* sorted_ids, int32_t* expert_ids,
                          int32_t* num_post_pad, int max_blocks, cudaStream_t stream);

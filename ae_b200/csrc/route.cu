@@ -173,6 +173,27 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       s_ids[f] = id;
       s_w[f] = w;
     });
+  } else if (a.ep_recv != nullptr) {
+    // expert side of the exchange: payload row f = s*C + i of source s belongs to the
+    // local expert whose run of the source's header counts holds i (k = 1, weight 1)
+    const size_t row_bytes = static_cast<size_t>(a.H) * 2;
+    for (int f = tid; f < Tk; f += kRouteThreads) {
+      const int src = f / a.ep_C;
+      const int i = f - src * a.ep_C;
+      const int32_t* hdr = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(a.ep_recv) +
+                                                            static_cast<size_t>(src) * (a.ep_C + 1) * row_bytes);
+      int id = -1, acc = 0;
+      for (int e = 0; e < a.ep_Eloc; ++e) {
+        const int c = hdr[e];
+        if (i < acc + c) {
+          id = e;
+          break;
+        }
+        acc += c;
+      }
+      s_ids[f] = id;
+      s_w[f] = 1.0f;
+    }
   } else {
     for (int f = tid; f < Tk; f += kRouteThreads) {
       int id = a.in_ids[f];
@@ -258,6 +279,16 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   // 5. outputs for this CTA's flat range
   if (blockIdx.x == 0) {
     for (int e = tid; e <= E; e += kRouteThreads) a.expert_off[e] = s_off[e];
+    if (a.ep_send != nullptr) {
+      // header row of each destination chunk: counts of that destination's experts
+      const size_t row_bytes = static_cast<size_t>(a.H) * 2;
+      for (int e = tid; e < E; e += kRouteThreads) {
+        const int d = e / a.ep_Eloc;
+        int32_t* hdr = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(a.ep_send) +
+                                                  static_cast<size_t>(d) * (a.ep_C + 1) * row_bytes);
+        hdr[e - d * a.ep_Eloc] = s_off[e + 1] - s_off[e];
+      }
+    }
     if (a.done != nullptr) {
       for (int e = tid; e <= E; e += kRouteThreads) a.done[e] = 0;
     }
@@ -273,10 +304,22 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
     if (a.out_w != nullptr) a.out_w[f] = s_w[f];
     if (a.out_ids != nullptr) a.out_ids[f] = s_ids[f];
   }
-  // token rows of this CTA's flat range into xp, all threads on all rows, four
-  // independent 16-byte loads in flight per thread
-  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
-  uint4* xdst = reinterpret_cast<uint4*>(a.xp);
+  // token rows of this CTA's flat range into xp (or into the exchange layout), all
+  // threads on all rows, four independent 16-byte loads in flight per thread
+  const uint4* xsrc = reinterpret_cast<const uint4*>(a.ep_recv != nullptr ? a.ep_recv : a.x);
+  uint4* xdst = reinterpret_cast<uint4*>(a.ep_send != nullptr ? a.ep_send : a.xp);
+  // source row of token t: plain, or payload row t of the exchange layout
+  auto src_row = [&](int t) -> size_t {
+    if (a.ep_recv == nullptr) return static_cast<size_t>(t);
+    const int s = t / a.ep_C;
+    return static_cast<size_t>(s) * (a.ep_C + 1) + 1 + (t - s * a.ep_C);
+  };
+  // destination row of flat slot f at expert-major position p
+  auto dst_row = [&](int f, int p) -> size_t {
+    if (a.ep_send == nullptr) return static_cast<size_t>(p);
+    const int d = s_ids[f] / a.ep_Eloc;
+    return static_cast<size_t>(d) * (a.ep_C + 1) + 1 + (p - s_off[d * a.ep_Eloc]);
+  };
   const int nvec = (g1 - g0) * vec_per_row;
   for (int base = tid; base < nvec; base += 4 * kRouteThreads) {
     uint4 v[4];
@@ -285,7 +328,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        if (s_pos[f] >= 0) v[j] = __ldg(xsrc + static_cast<size_t>(f / a.k) * vec_per_row + (i % vec_per_row));
+        if (s_pos[f] >= 0) v[j] = __ldg(xsrc + src_row(f / a.k) * vec_per_row + (i % vec_per_row));
       }
     }
 #pragma unroll
@@ -293,7 +336,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        if (s_pos[f] >= 0) xdst[static_cast<size_t>(s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
+        if (s_pos[f] >= 0) xdst[dst_row(f, s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
       }
     }
   }

@@ -498,23 +498,27 @@ def run_ep(args, cfg, rank, world, dev):
     clocks = sampler.summary(t_soak, t_end)
     sampler.stop()
 
-    # the local expert FFN of a step, timed alone (the dominant kernel of a rank)
-    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-    reps = 10
-    t_exp = 0.0
-    for _ in range(reps):
-        moe(x, logits, events=ev)
-        torch.cuda.synchronize(dev)
-        t_exp += ev[0].elapsed_time(ev[1]) / 1000.0
-    t_exp /= reps
-    rows, counts, state = moe.backend.route(x, logits)
-    rc = torch.empty(world * E_loc, dtype=torch.int32, device=dev)
-    dist.all_to_all_single(rc, counts.contiguous())
-    n_recv = int(rc.sum().item())
-    touched = int((rc.view(world, E_loc).sum(0) > 0).sum().item())
+    # the local expert FFN of a step on the rows this rank received, replayed from a
+    # graph and timed alone (the dominant work of a rank)
+    send, state = moe.backend.dispatch(x, logits, world, moe.C)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send)
+    torch.cuda.synchronize(dev)
+    hdr = recv.view(world, moe.C + 1, cfg.H)[:, 0].contiguous().view(torch.int32)[:, :E_loc].cpu()
+    n_recv = int(hdr.sum())
+    touched = int((hdr.sum(0) > 0).sum())
+
+    def experts():
+        moe.backend.experts(recv, world, moe.C, pool, moe.pages, E_loc)
+
+    g_exp = graph_of(experts, dev)
+    for _ in range(3):
+        g_exp.replay()
+    t_exp = timed_steps(g_exp.replay, 20, stream) / 20
     ffn_bytes = touched * 3 * cfg.H * cfg.I * 2 + n_recv * cfg.H * 2 * 2
     ach = torch.tensor([ffn_bytes / t_exp / 1e9], device=dev, dtype=torch.float64)
     dist.all_reduce(ach, op=dist.ReduceOp.MIN)
+    del g_exp
 
     # e2e through the public EP layer with host inputs and outputs, every step
     hx = x.cpu().pin_memory()
@@ -563,7 +567,8 @@ def run_ep(args, cfg, rank, world, dev):
                    "experts_per_gpu": E_loc, "parallelism": f"ep{world}",
                    "l2": "inputs larger than L2 (expert weights %.2f GB per GPU per step)"
                          % (cfg.weight_bytes(E_loc) / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": "local expert FFN (permute + ffn_gemm_kernel + combine), slowest rank",
+        "roofline": {"bound": "hbm", "kernel": "local experts on the received rows (smb_moe_ep_experts: "
+                                                "route_kernel + ffn_gemm_kernel + combine_kernel), slowest rank",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None},
         "cpu_baseline": None,

@@ -130,6 +130,36 @@ SMB_API int smb_moe_combine(void* out, int dtype, int T, int E, int k, int H, in
 SMB_API int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, int k, int H, int I,
                                  const void* ws, size_t ws_bytes, smb_stream_t stream);
 
+/* Expert parallelism over G ranks (E/G experts per rank).  Exchange layout: G chunks, one
+ * per peer rank, each of one header row plus C payload rows of H elements (storage
+ * dtype); a header row carries the chunk's per-local-expert row counts as int32 in its
+ * first (E/G)*4 bytes.  With C >= T*k (the worst case) nothing can overflow and the
+ * all-to-alls move fixed sizes, so no count has to reach the host.  The reference has
+ * no expert-parallel path (its ep flags are parsed but unused,
+ * specmoe/utils/server_args.py:148,202); these replace the TP all-reduce placement of
+ * specmoe/models/mixtral.py:113-114 for expert-sharded deployments.
+ *
+ * Source side, before the exchange: routing (as smb_moe_route) and the gather of token
+ * rows into send [G][C+1][H] (destination-major, headers filled). */
+SMB_API int smb_moe_ep_dispatch(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E,
+                                int k, int H, int I, int renormalize, int G, int C, void* send,
+                                float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes,
+                                smb_stream_t stream);
+
+/* Expert side: the received chunks recv [G][C+1][H] through this rank's E_loc experts
+ * (pool / page_of_expert hold the local pages); out_rows [G][C][H] gets each payload
+ * row's expert output (zero past a chunk's counts).  ws is sized for T = G*C, E = E_loc,
+ * k = 1 (smb_moe_workspace_bytes(G*C, E_loc, 1, H, I, dtype)). */
+SMB_API int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t num_pages,
+                               const int64_t* page_of_expert, int dtype, int E_loc, int H, int I, void* out_rows,
+                               void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* Source side, after the exchange: out[t] = sum_j w[t,j] * back[row of slot (t,j)], back
+ * [G][C][H] holding the returned expert outputs; ws is the workspace of the matching
+ * smb_moe_ep_dispatch call. */
+SMB_API int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int k, int H, int I, int G,
+                               int C, const void* ws, size_t ws_bytes, smb_stream_t stream);
+
 /* Whole layer: route + ffn + combine (FusedMoE.forward, FusedMoE.py:508-532, without
  * the tensor-parallel all-reduce).  out may alias x (the reference writes in place). */
 SMB_API int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,

@@ -17,36 +17,50 @@ from oracle import moe_oracle as mo
 
 
 class OracleBackend:
-    """The three compute steps of ae_b200.ep.CudaBackend, restated on the CPU."""
+    """The three compute steps of ae_b200.ep.CudaBackend, restated on the CPU, with the same
+    exchange layout: G chunks of [1 header row of int32 counts | C payload rows]."""
 
     def __init__(self, E, k, H, I, renormalize=True):
         self.E, self.k, self.H, self.I = E, k, H, I
         self.renormalize = renormalize
 
-    def route(self, x, logits):
+    def dispatch(self, x, logits, G, C):
+        T = x.shape[0]
+        E_loc = self.E // G
+        send = torch.zeros(G * (C + 1), self.H)
         w, ids = mo.select_experts(logits, self.k, self.renormalize)
         perm, off, inv = mo.permutation(ids, self.E)
-        rows = x[torch.from_numpy(perm).long() // self.k].contiguous()
-        counts = torch.from_numpy(np.diff(off)).to(torch.int32)
-        return rows, counts, (w, inv)
+        for d in range(G):
+            hdr = send[d * (C + 1)].view(torch.int32)
+            for el in range(E_loc):
+                e = d * E_loc + el
+                hdr[el] = int(off[e + 1] - off[e])
+            for p in range(off[d * E_loc], off[(d + 1) * E_loc]):
+                send[d * (C + 1) + 1 + p - off[d * E_loc]] = x[int(perm[p]) // self.k]
+        return send, (w, ids, inv, off)
 
-    def experts(self, rows, local_ids, pool, pages, num_local):
-        out = torch.zeros_like(rows)
-        for i in range(rows.shape[0]):
-            if int(local_ids[i]) < 0:  # padding row of the fixed-capacity exchange
-                continue
-            w1, w3, w2 = mo.page_views(pool[int(pages[int(local_ids[i])])], self.H, self.I)
-            a = torch.nn.functional.silu(w1 @ rows[i]) * (w3 @ rows[i])
-            out[i] = w2 @ a
+    def experts(self, recv, G, C, pool, pages, num_local):
+        out = torch.zeros(G * C, self.H)
+        for s in range(G):
+            counts = recv[s * (C + 1)].view(torch.int32)[:num_local].tolist()
+            i = 0
+            for el, c in enumerate(counts):
+                w1, w3, w2 = mo.page_views(pool[int(pages[el])], self.H, self.I)
+                for _ in range(c):
+                    row = recv[s * (C + 1) + 1 + i]
+                    out[s * C + i] = w2 @ (torch.nn.functional.silu(w1 @ row) * (w3 @ row))
+                    i += 1
         return out
 
-    def combine(self, back, state, T):
-        w, inv = state
+    def combine(self, back, state, T, G, C):
+        w, ids, inv, off = state
+        E_loc = self.E // G
         out = torch.zeros(T, self.H)
         for t in range(T):
             for j in range(self.k):
                 f = t * self.k + j
-                out[t] += float(w[t, j]) * back[int(inv[f])]
+                d = int(ids[t, j]) // E_loc
+                out[t] += float(w[t, j]) * back[d * C + int(inv[f]) - int(off[d * E_loc])]
         return out
 
 
