@@ -239,6 +239,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.xp = at<void>(ws, L.xp);
   a.status = at<int>(ws, L.status);
   a.done = at<int>(ws, L.done);
+  a.done_count = E * L.splits + 1;
   a.ep_send = ep.send;
   a.ep_recv = ep.recv;
   a.ep_G = ep.G;
@@ -280,7 +281,7 @@ int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, i
   args.page_of_expert = page_of_expert;
   args.status = at<int>(ws, L.status);
   args.done = at<int>(ws, L.done);
-  args.sched = at<int>(ws, L.done) + E;
+  args.sched = at<int>(ws, L.done) + E * L.splits;
   args.xp = at<void>(ws, L.xp);
   args.a2 = at<void>(ws, L.a2);
   args.part = at<float>(ws, L.part);
@@ -293,7 +294,7 @@ int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, i
   args.phase_mask = phases;
   if (!counters_zeroed) {
     // standalone call: the router zeroed the counters for the first FFN launch only
-    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (E + 1), stream);
+    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (static_cast<size_t>(E) * L.splits + 1), stream);
     if (err != cudaSuccess) return cuda_fail(err);
   }
   cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, args);

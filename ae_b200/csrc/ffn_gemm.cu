@@ -109,16 +109,30 @@ __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
     r.kb0 = 0;
     r.kb1 = g.kb1_total;
   } else {
+    // expert-major like the gate/up units, then split, then row tile: an expert's first
+    // down units read only its first features, whose gate/up units finish first
     const int v = u - g.n1;
+    const int per_expert = g.m2 * g.splits;
     r.phase = 2;
-    r.ks = v % g.splits;
-    const int q = v / g.splits;
-    r.te = q / g.m2;
+    r.te = v / per_expert;
+    const int q = v - r.te * per_expert;
+    r.ks = q / g.m2;
     r.mt = q % g.m2;
     r.kb0 = static_cast<int>((static_cast<long long>(g.kb2_total) * r.ks) / g.splits);
     r.kb1 = static_cast<int>((static_cast<long long>(g.kb2_total) * (r.ks + 1)) / g.splits);
   }
   return r;
+}
+
+// K blocks [kb0, kb1) of split ks of the down projection (64-wide blocks of I).
+__device__ __forceinline__ int split_kb0(const Geometry& g, int ks) {
+  return static_cast<int>((static_cast<long long>(g.kb2_total) * ks) / g.splits);
+}
+// Gate/up units (128 features = 2 K blocks of the down projection each) a down unit of
+// split ks waits for: those whose features overlap the split's K range.
+__device__ __forceinline__ int split_need(const Geometry& g, int ks) {
+  const int b0 = split_kb0(g, ks), b1 = split_kb0(g, ks + 1);
+  return min(g.m1, (b1 + 1) / 2) - b0 / 2;
 }
 
 }  // namespace
@@ -403,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const uint64_t t0 = global_timer_ns();
           while (true) {
-            if (ld_acquire(args.done + e) >= g.m1) {
+            if (ld_acquire(args.done + e * g.splits + un.ks) >= split_need(g, un.ks)) {
               ready = 1;
               break;
             }
@@ -514,10 +528,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&tempty_bar[buf]);
       }
       if (ok && un.phase == 1 && chained) {
-        // publish: this unit's A2 columns are written (release at GPU scope)
+        // publish: this unit's A2 columns are written (release at GPU scope); count it
+        // for every down split whose K range overlaps its 128 features
         __threadfence();
         named_bar_sync(1, 128);
-        if (et == 0) atomicAdd(args.done + e, 1);
+        if (et == 0) {
+          const int f0 = un.mt * 2, f1 = min(un.mt * 2 + 2, g.kb2_total);
+          for (int ks = 0; ks < g.splits; ++ks) {
+            if (f0 < split_kb0(g, ks + 1) && f1 > split_kb0(g, ks)) atomicAdd(args.done + e * g.splits + ks, 1);
+          }
+        }
       }
     }
   }

@@ -32,7 +32,7 @@ struct FfnArgs {
   const int32_t* expert_off;      // [E+1]
   const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
   int* status;                    // device status word
-  int* done;                      // [E] finished gate/up units per expert (zeroed by the router)
+  int* done;                      // [E*S] finished gate/up units per (expert, down split), zeroed by the router
   int* sched;                     // [1] next unit to hand out (zeroed by the router)
   const void* xp;                 // [rows, H] token rows, expert-major
   void* a2;                       // [rows, I] activations, expert-major
@@ -61,7 +61,8 @@ struct RouteArgs {
   int32_t* ws_ids;
   void* xp;
   int* status;
-  int* done;               // [E+1] per-expert counters + work counter of the FFN kernel, zeroed here
+  int* done;               // [done_count] counters of the FFN kernel (see WsLayout::done), zeroed here
+  int done_count;
   int rows_per_cta;
   // expert-parallel exchange layout: G chunks of (1 header row + C payload rows) x H; a
   // header row holds the chunk's per-local-expert counts as int32 in its first bytes

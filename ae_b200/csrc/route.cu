@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       }
     }
     if (a.done != nullptr) {
-      for (int e = tid; e <= E; e += kRouteThreads) a.done[e] = 0;
+      for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
     }
   }
   const int g0 = min(Tk, static_cast<int>(blockIdx.x) * a.rows_per_cta);

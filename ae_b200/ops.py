@@ -248,7 +248,7 @@ class StagedLayer:
         S = splits(E, H, I, Tk)
         o = 0
         off = {}
-        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E + 1)), ("perm", 4 * Tk),
+        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E * S + 1)), ("perm", 4 * Tk),
                          ("inv", 4 * Tk),
                          ("w", 4 * Tk), ("ids", 4 * Tk), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
                          ("part", 4 * S * Tk * H)):
@@ -263,7 +263,7 @@ class StagedLayer:
         return {
             "expert_off": view("expert_off", torch.int32, (E + 1,)),
             "status": view("status", torch.int32, (8,)),
-            "done": view("done", torch.int32, (E + 1,)),
+            "done": view("done", torch.int32, (E * S + 1,)),
             "perm": view("perm", torch.int32, (Tk,)),
             "inv": view("inv", torch.int32, (Tk,)),
             "w": view("w", torch.float32, (Tk,)),
