@@ -27,8 +27,8 @@ SIGNATURES = {
     "smb_moe_splits": (_I, [_I, _I, _I, _I]),
     "smb_moe_route": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
     "smb_moe_permute": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
-    "smb_moe_ffn": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
-    "smb_moe_gate_up": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_ffn": (_I, [_P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_gate_up": (_I, [_P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_down": (_I, [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_combine": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_combine_rows": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),

@@ -188,7 +188,10 @@ int encode_2d_uncached(CUtensorMap* map, const void* base, int dtype, uint64_t r
   return r == CUDA_SUCCESS ? SMB_OK : SMB_ERR_TMA;
 }
 
-int route_grid(int Tk, int sms) {
+// The router gathers token rows only into the expert-parallel send buffer; then the
+// copy is spread over CTAs (8 rows each).  Otherwise one CTA routes and permutes.
+int route_grid(int Tk, int sms, bool gathers) {
+  if (!gathers) return 1;
   int g = (Tk + 7) / 8;
   if (g < 1) g = 1;
   if (g > sms) g = sms;
@@ -236,17 +239,16 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.inv = at<int32_t>(ws, L.inv);
   a.ws_w = at<float>(ws, L.w);
   a.ws_ids = at<int32_t>(ws, L.ids);
-  a.xp = at<void>(ws, L.xp);
   a.status = at<int>(ws, L.status);
   a.done = at<int>(ws, L.done);
-  a.done_count = E * L.splits + 1;
+  a.done_count = E * L.splits + 2;
   a.ep_send = ep.send;
   a.ep_recv = ep.recv;
   a.ep_G = ep.G;
   a.ep_C = ep.C;
   a.ep_Eloc = ep.Eloc;
   const int Tk = T * k;
-  const int grid = route_grid(Tk, di.sms);
+  const int grid = route_grid(Tk, di.sms, ep.send != nullptr);
   a.rows_per_cta = (Tk + grid - 1) / grid;
   cudaError_t err = launch_route(a, elem_bytes_of(dtype), grid, stream, pdl_enabled());
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
@@ -254,14 +256,16 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
 
 // phase bit 1: gate/up GEMM (+SiLU*mul), bit 2: down GEMM (split-K partials); both bits
 // run both phases in one persistent launch.
-int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k,
-           int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases, bool counters_zeroed) {
+int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
+           int T, int E, int k, int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases,
+           bool counters_zeroed) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
   if (T == 0) return SMB_OK;
   if (pool == nullptr || page_of_expert == nullptr) return SMB_ERR_NULL;
-  if (!aligned(pool, 16)) return SMB_ERR_ALIGN;
+  if ((phases & 1) && x == nullptr) return SMB_ERR_NULL;
+  if (!aligned(pool, 16) || !aligned(x, 16)) return SMB_ERR_ALIGN;
   if (num_pages < 1) return SMB_ERR_SHAPE;
   const long long rows1 = static_cast<long long>(num_pages) * 3 * I;
   const long long rows2 = static_cast<long long>(num_pages) * 3 * H;
@@ -282,6 +286,10 @@ int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, i
   args.status = at<int>(ws, L.status);
   args.done = at<int>(ws, L.done);
   args.sched = at<int>(ws, L.done) + E * L.splits;
+  args.x = x;
+  args.x_chunk = x_chunk;
+  args.inv = at<int32_t>(ws, L.inv);
+  args.k = k;
   args.xp = at<void>(ws, L.xp);
   args.a2 = at<void>(ws, L.a2);
   args.part = at<float>(ws, L.part);
@@ -294,7 +302,7 @@ int do_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, i
   args.phase_mask = phases;
   if (!counters_zeroed) {
     // standalone call: the router zeroed the counters for the first FFN launch only
-    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (static_cast<size_t>(E) * L.splits + 1), stream);
+    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (static_cast<size_t>(E) * L.splits + 2), stream);
     if (err != cudaSuccess) return cuda_fail(err);
   }
   cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, args);
@@ -378,21 +386,21 @@ int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, const vo
                   ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int smb_moe_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
-                int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
-  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+int smb_moe_ffn(const void* x, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
+                int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  return do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
                 reinterpret_cast<cudaStream_t>(stream), 3, false);
 }
 
-int smb_moe_gate_up(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
-                    int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
-  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+int smb_moe_gate_up(const void* x, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
+                    int T, int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  return do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
                 reinterpret_cast<cudaStream_t>(stream), 1, false);
 }
 
 int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
                  int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream) {
-  return do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
+  return do_ffn(nullptr, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes,
                 reinterpret_cast<cudaStream_t>(stream), 2, false);
 }
 
@@ -446,7 +454,7 @@ int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t
   int rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
                     ws_bytes, s, ep);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
+  rc = do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out_rows, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s);
 }
@@ -475,7 +483,7 @@ int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, 
   int rc = smb_moe_route(router_logits, logits_dtype, x, dtype, T, E, k, H, I, renormalize, topk_weights,
                          topk_ids, ws, ws_bytes, stream);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
+  rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }
@@ -486,7 +494,7 @@ int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = smb_moe_permute(topk_weights, topk_ids, x, dtype, T, E, k, H, I, ws, ws_bytes, stream);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
+  rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }

@@ -25,7 +25,9 @@
 // Data movement.  Each SM's TMA engine delivers about 50 GB/s; 148 SMs together
 // saturate HBM only if TMA moves nothing but weights.  So weights come by TMA in 16 KB
 // boxes (128 rows x 64 K, 128-byte swizzle, evict-first) and the small, L2-resident token
-// tiles come by cp.async from two loader warps, written in the same swizzled layout.
+// tiles come by cp.async from two loader warps, written in the same swizzled layout.  The
+// gate/up token rows are first gathered into expert-major order by all CTAs in the
+// prologue (a grid counter tells the loaders when it is complete), the down rows are A2.
 //
 // Roles (256 threads, one CTA per SM):
 //   warp 0      TMA producer (one thread): weight boxes, 32 KB per stage
@@ -57,15 +59,19 @@ constexpr int kMaxStages = 8;
 constexpr int kLoaderThreads = 64;
 constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
 constexpr int kQueueReaders = 4;               // MMA thread, the two loader-warp leaders, epilogue leader
-constexpr int kDynSmem = 227 * 1024 - 3072;
+constexpr int kDynSmem = 227 * 1024 - 4096;  // static shared block (~3.5 KB) + this <= 227 KB
 constexpr int kPrefetchBlocks = 16;            // K blocks of the first unit warmed in L2 (512 KB)
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+// 16-byte copy global -> shared (zero-filled when !valid), with an L2 eviction policy:
+// token rows are re-read by every weight tile of their expert, so they are kept in L2
+// ahead of the streamed weights.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0), "l"(pol)
                : "memory");
 }
 // Arrive on `bar` once every cp.async this thread issued so far has landed; the
@@ -76,6 +82,16 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_evict_last(float* p, float v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void st_evict_last(__nv_bfloat16* p, __nv_bfloat16 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.b16 [%0], %1, %2;" ::"l"(p), "h"(__bfloat16_as_ushort(v)), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void st_evict_last(__half* p, __half v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.b16 [%0], %1, %2;" ::"l"(p), "h"(__half_as_ushort(v)), "l"(pol) : "memory");
 }
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -245,6 +261,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   pdl_launch_dependents();
 
+  // Gather: token rows into xp in expert-major order, each CTA a contiguous share of
+  // the flat slots (slot f -> position inv[f], token f / k; in the expert-parallel
+  // exchange layout token t is payload row t of chunk t / C).  The CTA then counts
+  // itself in (release); token loaders wait for all CTAs before the first gate/up tile,
+  // while the weight stream has already started.  Skipped when only the down phase runs.
+  if (do1) {
+    const int Tk = args.Tk;
+    const int per = (Tk + gridDim.x - 1) / gridDim.x;
+    const int f0 = min(Tk, static_cast<int>(blockIdx.x) * per), f1 = min(Tk, f0 + per);
+    const int vec = H * static_cast<int>(sizeof(T)) / 16;
+    const uint4* xs = reinterpret_cast<const uint4*>(args.x);
+    uint4* xd = reinterpret_cast<uint4*>(args.xp);
+    const int nvec = (f1 - f0) * vec;
+    for (int i = threadIdx.x; i < nvec; i += kThreads) {
+      const int f = f0 + i / vec;
+      const int p = args.inv[f];
+      if (p < 0 || p >= Tk) continue;
+      const int t = f / args.k;
+      const int srow = args.x_chunk == 0 ? t : (t / args.x_chunk) * (args.x_chunk + 1) + 1 + (t % args.x_chunk);
+      xd[static_cast<size_t>(p) * vec + (i % vec)] = __ldg(xs + static_cast<size_t>(srow) * vec + (i % vec));
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(args.sched + 1, 1);
+  }
+
   const uint32_t tmem = s_tmem;
   const int ncap = s_ncap;
   const int nstages = s_stages;
@@ -391,9 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ token-tile loaders
     // Lane 0 of each loader warp does every wait and broadcasts the outcome, so a wait
     // that gives up ends the whole warp together.
+    // Gate/up token rows come from xp (gathered in this kernel's prologue, see above),
+    // down rows from A2; both in expert-major order, rows row0 + n0 + r.
     const int bt = threadIdx.x - 64;
     const T* xp = reinterpret_cast<const T*>(args.xp);
     const T* a2 = reinterpret_cast<const T*>(args.a2);
+    const uint64_t pol_rows = policy_evict_last();
+    bool gathered = false;
     const unsigned full = 0xffffffffu;
     int stage = 0;
     uint32_t phase = 0;
@@ -409,7 +455,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = s_touched[un.te];
       const int row0 = args.expert_off[e];
       const int n_e = args.expert_off[e + 1] - row0;
-      const T* src = un.phase == 1 ? xp : a2;
       const int K = un.phase == 1 ? H : I;
       if (un.phase == 2 && chained) {
         // A2 rows of expert e are complete once all its gate/up units have counted in
@@ -435,6 +480,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
         const int nlen = min(ncap, n_e - n0);
         const int nb = (nlen + 15) & ~15;
+        if (un.phase == 1 && !gathered) {
+          // every CTA's share of xp must be written before the first gate/up tile
+          int ready = 0;
+          if (lane == 0) {
+            const uint64_t t0 = global_timer_ns();
+            while (true) {
+              if (ld_acquire(args.sched + 1) >= static_cast<int>(gridDim.x)) {
+                ready = 1;
+                break;
+              }
+              if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+              if (global_timer_ns() - t0 > kWaitBudgetNs) {
+                record_status(args.status, kDevTimeout);
+                s_abort = 1;
+                break;
+              }
+            }
+          }
+          ready = __shfl_sync(full, ready, 0);
+          if (!ready) {
+            ok = false;
+            break;
+          }
+          gathered = true;
+        }
+        const T* src = un.phase == 1 ? xp : a2;
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           int got = 0;
           if (lane == 0) got = mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort) ? 1 : 0;
@@ -450,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int q = c & 7;
             const bool valid = r < nlen;
             const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
-            cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid);
+            cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid, pol_rows);
           }
           cp_async_arrive_noinc(&fullB_bar[stage]);
           if (++stage == nstages) {
@@ -466,6 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = warp & 3;          // TMEM lane quarter this warp may read
     const int row = sub * 32 + lane;   // accumulator row = TMEM lane
     const int et = threadIdx.x - 128;  // 0..127
+    // A2 rows are read back by the down units and the partials by the combine moments
+    // later; keep them in L2 while the weight stream (evict-first) passes through
+    const uint64_t pol_keep = policy_evict_last();
     int qi = 0;
     uint32_t qph = 0;
     int pass = 0;
@@ -506,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 16; ++i) {
                 const int p = row0 + n0 + c0 + i;
                 if (c0 + i < nlen && p >= 0 && p < args.Tk) {
-                  out[static_cast<size_t>(p) * I + f] = from_f32<T>(silu_f32(va[i]) * vb[i]);
+                  st_evict_last(out + static_cast<size_t>(p) * I + f, from_f32<T>(silu_f32(va[i]) * vb[i]), pol_keep);
                 }
               }
             }
@@ -518,8 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int p = row0 + n0 + c0 + i;
               if (c0 + i < nlen && p >= 0 && p < args.Tk) {
                 float* dst = args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H;
-                if (h0 < H) dst[h0] = va[i];
-                if (h1 < H) dst[h1] = vb[i];
+                if (h0 < H) st_evict_last(dst + h0, va[i], pol_keep);
+                if (h1 < H) st_evict_last(dst + h1, vb[i], pol_keep);
               }
             }
           }

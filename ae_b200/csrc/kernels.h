@@ -33,8 +33,12 @@ struct FfnArgs {
   const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
   int* status;                    // device status word
   int* done;                      // [E*S] finished gate/up units per (expert, down split), zeroed by the router
-  int* sched;                     // [1] next unit to hand out (zeroed by the router)
-  const void* xp;                 // [rows, H] token rows, expert-major
+  int* sched;                     // [2] next unit to hand out, CTAs done gathering (zeroed by the router)
+  const void* x;                  // token rows: the layer input [T, H], or the exchange layout
+  int x_chunk;                    // 0: row t of x; C > 0: payload row t of [G][C+1][H]
+  const int32_t* inv;             // [Tk] expert-major position of each flat slot
+  int k;                          // top-k (slot f belongs to token f / k)
+  void* xp;                       // [rows, H] gathered token rows, expert-major
   void* a2;                       // [rows, I] activations, expert-major
   float* part;                    // [S, Tk, H] split-K partials of the down projection
   long long num_pages;            // P
@@ -59,14 +63,13 @@ struct RouteArgs {
   int32_t* inv;
   float* ws_w;
   int32_t* ws_ids;
-  void* xp;
   int* status;
   int* done;               // [done_count] counters of the FFN kernel (see WsLayout::done), zeroed here
   int done_count;
   int rows_per_cta;
   // expert-parallel exchange layout: G chunks of (1 header row + C payload rows) x H; a
   // header row holds the chunk's per-local-expert counts as int32 in its first bytes
-  void* ep_send;           // dispatch: gather rows here (dst-major, capacity C) instead of xp
+  void* ep_send;           // dispatch: gather rows here (dst-major, capacity C)
   const void* ep_recv;     // receive: tokens are the payload rows, ids come from the headers
   int ep_G, ep_C, ep_Eloc;
 };

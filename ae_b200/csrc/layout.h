@@ -26,12 +26,13 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct WsLayout {
   size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert
   size_t status;      // int32 [8]     device status word(s)
-  size_t done;        // int32 [E*S+1] finished gate/up units per (expert, down split), then the FFN work counter
+  size_t done;        // int32 [E*S+2] finished gate/up units per (expert, down split), then the FFN work
+                      //               counter and the count of CTAs done gathering xp
+  size_t xp;          // elem  [rows, H] token rows in expert-major order (gathered by the FFN kernel)
   size_t perm;        // int32 [Tk]    perm[p] = flat slot f = t*k + j at position p
   size_t inv;         // int32 [Tk]    inv[f] = p
   size_t w;           // fp32  [Tk]    routing weight of flat slot f
   size_t ids;         // int32 [Tk]    expert of flat slot f
-  size_t xp;          // elem  [rows, H] token rows in expert-major order
   size_t a2;          // elem  [rows, I] silu(x W1^T) * (x W3^T) in expert-major order
   size_t part;        // fp32  [S, Tk, H] split-K partials of the down projection
   size_t total;
@@ -47,7 +48,7 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   size_t o = 0;
   L.expert_off = o; o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
   L.status = o;     o = align_up(o + sizeof(int32_t) * 8, kAlign);
-  L.done = o;       o = align_up(o + sizeof(int32_t) * (static_cast<size_t>(E) * splits + 1), kAlign);
+  L.done = o;       o = align_up(o + sizeof(int32_t) * (static_cast<size_t>(E) * splits + 2), kAlign);
   L.perm = o;       o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.inv = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.w = o;          o = align_up(o + sizeof(float) * Tk, kAlign);

@@ -1,4 +1,4 @@
-// Router + permutation + token gather, one launch.
+// Router + permutation, one launch.
 //
 // Reference semantics:
 //  * routing = sglang select_experts as called at specmoe/layers/FusedMoE.py:174-185
@@ -7,13 +7,12 @@
 //    specmoe/layers/fused_moe_kernel.py:19-55 without the block padding: flat slots
 //    f = t*k + j bucketed by expert, ascending f inside an expert.
 //
-// Every CTA recomputes the routing of all T tokens (one warp per token, logits in
-// registers, warp-shuffle argmax with ties to the lower expert) and the expert-major
-// positions (per-warp histograms, a scan, then match_any ranks inside 32-slot chunks).
-// For verify-sized batches this costs a few kilobytes of L2 reads per CTA and removes
-// every inter-CTA dependency.  Each CTA then owns a contiguous range of flat slots:
-// it writes their routing outputs and copies their token rows into the expert-major
-// buffer xp that the gate/up GEMM streams with TMA.
+// One CTA routes every token (a group of lanes per token, logits in registers,
+// shuffle argmax with ties to the lower expert) and computes the expert-major positions
+// (per-warp histograms, a scan, then match_any ranks inside 32-slot chunks).  The FFN
+// kernel reads token rows through the permutation, so nothing is copied here, except
+// for the expert-parallel dispatch: then every CTA recomputes the (cheap) routing and
+// copies its share of the token rows into the send buffer of the exchange.
 #include <cfloat>
 #include <climits>
 
@@ -304,10 +303,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
     if (a.out_w != nullptr) a.out_w[f] = s_w[f];
     if (a.out_ids != nullptr) a.out_ids[f] = s_ids[f];
   }
-  // token rows of this CTA's flat range into xp (or into the exchange layout), all
-  // threads on all rows, four independent 16-byte loads in flight per thread
+  // expert-parallel dispatch: token rows of this CTA's flat range into the exchange
+  // layout, all threads on all rows, four independent 16-byte loads in flight per thread
+  if (a.ep_send == nullptr) return;  // the FFN reads token rows through the permutation
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.ep_recv != nullptr ? a.ep_recv : a.x);
-  uint4* xdst = reinterpret_cast<uint4*>(a.ep_send != nullptr ? a.ep_send : a.xp);
+  uint4* xdst = reinterpret_cast<uint4*>(a.ep_send);
   // source row of token t: plain, or payload row t of the exchange layout
   auto src_row = [&](int t) -> size_t {
     if (a.ep_recv == nullptr) return static_cast<size_t>(t);

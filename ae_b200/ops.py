@@ -212,12 +212,12 @@ class StagedLayer:
         _native.call("smb_moe_permute", topk_weights.data_ptr(), topk_ids.data_ptr(), x.data_ptr(), self.code,
                      self.T, self.E, self.k, self.H, self.I, self.ws.data_ptr(), self.nbytes, self._s())
 
-    def ffn(self, pool, page_of_expert):
-        _native.call("smb_moe_ffn", pool.data_ptr(), pool.shape[0], page_of_expert.data_ptr(), self.code,
+    def ffn(self, pool, page_of_expert, x):
+        _native.call("smb_moe_ffn", x.data_ptr(), pool.data_ptr(), pool.shape[0], page_of_expert.data_ptr(), self.code,
                      self.T, self.E, self.k, self.H, self.I, self.ws.data_ptr(), self.nbytes, self._s())
 
-    def gate_up(self, pool, page_of_expert):
-        _native.call("smb_moe_gate_up", pool.data_ptr(), pool.shape[0], page_of_expert.data_ptr(), self.code,
+    def gate_up(self, pool, page_of_expert, x):
+        _native.call("smb_moe_gate_up", x.data_ptr(), pool.data_ptr(), pool.shape[0], page_of_expert.data_ptr(), self.code,
                      self.T, self.E, self.k, self.H, self.I, self.ws.data_ptr(), self.nbytes, self._s())
 
     def down(self, pool, page_of_expert):
@@ -248,7 +248,7 @@ class StagedLayer:
         S = splits(E, H, I, Tk)
         o = 0
         off = {}
-        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E * S + 1)), ("perm", 4 * Tk),
+        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E * S + 2)), ("perm", 4 * Tk),
                          ("inv", 4 * Tk),
                          ("w", 4 * Tk), ("ids", 4 * Tk), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
                          ("part", 4 * S * Tk * H)):
@@ -263,7 +263,7 @@ class StagedLayer:
         return {
             "expert_off": view("expert_off", torch.int32, (E + 1,)),
             "status": view("status", torch.int32, (8,)),
-            "done": view("done", torch.int32, (E * S + 1,)),
+            "done": view("done", torch.int32, (E * S + 2,)),
             "perm": view("perm", torch.int32, (Tk,)),
             "inv": view("inv", torch.int32, (Tk,)),
             "w": view("w", torch.float32, (Tk,)),

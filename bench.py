@@ -313,13 +313,13 @@ def run_ours(args, cfg, rank, world, dev):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.staged_steps)]
     for i in range(3):
         L.route(logits, x, cfg.renormalize)
-        L.ffn(pool, pages)
+        L.ffn(pool, pages, x)
         L.combine(out)
     for e in evs:
         e[0].record(stream)
         L.route(logits, x, cfg.renormalize)
         e[1].record(stream)
-        L.ffn(pool, pages)
+        L.ffn(pool, pages, x)
         e[2].record(stream)
         L.combine(out)
         e[3].record(stream)
@@ -615,6 +615,9 @@ def main():
     torch.cuda.set_device(dev)
     if world > 1:
         import torch.distributed as dist
+        # NCCL's own log lines (e.g. its version banner) go to stderr: stdout carries only
+        # rank 0's JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         dist.barrier()
     try:

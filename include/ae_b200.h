@@ -82,8 +82,7 @@ SMB_API size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dt
 SMB_API int smb_moe_splits(int E, int H, int I, int Tk);
 
 /* Router: softmax over E in fp32, top-k (ties to the lower expert index), optional
- * renormalisation; then the expert-major permutation and the gather of token rows into
- * the workspace.  Replaces select_experts (FusedMoE.py:174-185) + moe_align_block_size
+ * renormalisation; then the expert-major permutation (positions in the workspace).  Replaces select_experts (FusedMoE.py:174-185) + moe_align_block_size
  * (fused_moe_kernel.py:329).  topk_weights [T,k] fp32 / topk_ids [T,k] int32 are optional
  * outputs (NULL to skip). */
 SMB_API int smb_moe_route(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
@@ -95,7 +94,7 @@ SMB_API int smb_moe_route(const void* router_logits, int logits_dtype, const voi
 SMB_API int smb_moe_topk(const void* router_logits, int logits_dtype, int T, int E, int k, int renormalize,
                  float* topk_weights, int32_t* topk_ids, smb_stream_t stream);
 
-/* Permutation + gather from a routing computed elsewhere (stack_fused_moe's
+/* Permutation from a routing computed elsewhere (stack_fused_moe's
  * topk_weights / topk_ids arguments, fused_moe_kernel.py:257-259).  An id of -1 marks a
  * slot with no expert: it is left out of the permutation and contributes nothing to the
  * output (the padding rows of the expert-parallel exchange use it). */
@@ -104,15 +103,19 @@ SMB_API int smb_moe_permute(const float* topk_weights, const int32_t* topk_ids, 
 
 /* Expert FFN on the permuted rows: tcgen05 gate/up GEMM with SiLU*mul epilogue, then the
  * split-K down GEMM.  Replaces fused_moe_kernel GEMM1 + silu_and_mul + GEMM2
- * (fused_moe_kernel.py:332-342).  Needs smb_moe_route or smb_moe_permute first. */
-SMB_API int smb_moe_ffn(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E,
-                int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+ * (fused_moe_kernel.py:332-342).  Needs smb_moe_route or smb_moe_permute first, with the
+ * same x [T,H]: token rows are read from x through the permutation, so x must be
+ * unchanged between the two calls. */
+SMB_API int smb_moe_ffn(const void* x, const void* pool, int64_t num_pages, const int64_t* page_of_expert,
+                        int dtype, int T, int E, int k, int H, int I, void* ws, size_t ws_bytes,
+                        smb_stream_t stream);
 
 /* The two halves of smb_moe_ffn, for callers that interleave other work or time them
  * separately: the gate/up GEMM with the SiLU*mul epilogue (fused_moe_kernel.py:332-337)
  * and the split-K down GEMM (fused_moe_kernel.py:339-342). */
-SMB_API int smb_moe_gate_up(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
-                            int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
+SMB_API int smb_moe_gate_up(const void* x, const void* pool, int64_t num_pages, const int64_t* page_of_expert,
+                            int dtype, int T, int E, int k, int H, int I, void* ws, size_t ws_bytes,
+                            smb_stream_t stream);
 SMB_API int smb_moe_down(const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
                          int E, int k, int H, int I, void* ws, size_t ws_bytes, smb_stream_t stream);
 
