@@ -79,3 +79,15 @@ def make_inputs(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, T: 
         ranks = torch.randperm(cfg.E, generator=g, device=device).float()
         logits = logits + (-cfg.zipf_s * torch.log(ranks + 1.0)).unsqueeze(0)
     return x.to(dtype), logits.to(dtype)
+
+
+def make_gate_inputs(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, T: int | None = None):
+    """(x [T,H], gate weight [E,H]) in the storage dtype for the gated block
+    (``MixtralMoE``: router logits = x @ W^T computed by the layer itself); same statistics
+    as :func:`make_inputs` without the Zipf bias (the reference gate has no bias)."""
+    T = cfg.T if T is None else T
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 7919 + 17)
+    x = torch.randn(T, cfg.H, generator=g, device=device, dtype=torch.float32)
+    wr = torch.randn(cfg.E, cfg.H, generator=g, device=device, dtype=torch.float32) * cfg.router_std
+    return x.to(dtype), wr.to(dtype)

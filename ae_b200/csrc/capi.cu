@@ -198,15 +198,27 @@ int route_grid(int Tk, int sms, bool gathers) {
   return g;
 }
 
+// Gate CTAs: every CTA takes ceil(T / SMs) consecutive tokens, no CTA is left empty.
+int gate_grid(int T, int sms) {
+  const int per = (T + sms - 1) / sms;
+  return (T + per - 1) / per;
+}
+
 struct EpLayout {
   void* send = nullptr;        // dispatch: write rows into [G][C+1][H]
   const void* recv = nullptr;  // experts: tokens are the payload rows of [G][C+1][H]
   int G = 0, C = 0, Eloc = 1;
 };
 
+// Router gate inputs of the gated launch (x is the token matrix passed to do_route).
+struct GateIn {
+  const void* weight = nullptr;  // [E, H] storage dtype
+  void* logits_out = nullptr;    // optional [T, E] storage dtype
+};
+
 int do_route(const void* logits, int logits_dtype, const float* in_w, const int32_t* in_ids, const void* x,
              int dtype, int T, int E, int k, int H, int I, int renorm, float* out_w, int32_t* out_ids, void* ws,
-             size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout()) {
+             size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout(), const GateIn* gate = nullptr) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
@@ -215,8 +227,11 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
     return SMB_ERR_DTYPE;
   if (T == 0) return SMB_OK;
   if (x == nullptr) return SMB_ERR_NULL;
-  if (logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr)) return SMB_ERR_NULL;
+  if (gate == nullptr && logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr))
+    return SMB_ERR_NULL;
+  if (gate != nullptr && (gate->weight == nullptr || ep.send != nullptr || ep.recv != nullptr)) return SMB_ERR_NULL;
   if (!aligned(x, 16)) return SMB_ERR_ALIGN;
+  if (gate != nullptr && !aligned(gate->weight, 16)) return SMB_ERR_ALIGN;
   DeviceInfo di;
   rc = device_info(&di);
   if (rc != SMB_OK) return rc;
@@ -248,6 +263,25 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.ep_C = ep.C;
   a.ep_Eloc = ep.Eloc;
   const int Tk = T * k;
+  if (gate != nullptr) {
+    // gate + routing in one launch: the gate's CTAs each take ceil(T / SMs) tokens, the
+    // last CTA to finish routes every token from the logits in the workspace
+    GateArgs g{};
+    g.x = x;
+    g.weight = gate->weight;
+    g.logits = at<float>(ws, L.logits);
+    g.logits_out = gate->logits_out;
+    g.ticket = at<int>(ws, L.status) + 1;
+    g.T = T;
+    g.E = E;
+    g.H = H;
+    g.route = 1;
+    a.logits = g.logits;
+    a.logits_dtype = SMB_DTYPE_F32;
+    a.rows_per_cta = Tk;
+    cudaError_t err = launch_gate_route(a, g, dtype, gate_grid(T, di.sms), stream, pdl_enabled());
+    return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+  }
   const int grid = route_grid(Tk, di.sms, ep.send != nullptr);
   a.rows_per_cta = (Tk + grid - 1) / grid;
   cudaError_t err = launch_route(a, elem_bytes_of(dtype), grid, stream, pdl_enabled());
@@ -493,6 +527,61 @@ int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32
                            int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = smb_moe_permute(topk_weights, topk_ids, x, dtype, T, E, k, H, I, ws, ws_bytes, stream);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
+}
+
+int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (ws == nullptr) return SMB_ERR_NULL;
+  if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
+  if (ws_bytes < kWsHeaderBytes) return SMB_ERR_WORKSPACE;
+  cudaError_t err = cudaMemsetAsync(ws, 0, kWsHeaderBytes, reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_gate(const void* x, const void* gate_weight, int dtype, int T, int E, int H, void* router_logits,
+                 smb_stream_t stream) {
+  if (elem_bytes_of(dtype) == 0) return SMB_ERR_DTYPE;
+  if (T < 0 || E < 1 || E > kMaxExperts || H < 128 || H % 128 != 0) return SMB_ERR_SHAPE;
+  if (T == 0) return SMB_OK;
+  if (x == nullptr || gate_weight == nullptr || router_logits == nullptr) return SMB_ERR_NULL;
+  if (!aligned(x, 16) || !aligned(gate_weight, 16)) return SMB_ERR_ALIGN;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != SMB_OK) return rc;
+  if (!di.sm100) return SMB_ERR_ARCH;
+  RouteArgs a{};
+  a.T = T;
+  a.E = E;
+  a.k = 1;
+  a.H = H;
+  GateArgs g{};
+  g.x = x;
+  g.weight = gate_weight;
+  g.logits_out = router_logits;
+  g.T = T;
+  g.E = E;
+  g.H = H;
+  g.route = 0;
+  g.logits = nullptr;  // logits only: no workspace copy, no routing
+  cudaError_t err =
+      launch_gate_route(a, g, dtype, gate_grid(T, di.sms), reinterpret_cast<cudaStream_t>(stream), pdl_enabled());
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_forward_gated(const void* x, const void* gate_weight, const void* pool, int64_t num_pages,
+                          const int64_t* page_of_expert, int dtype, int T, int E, int k, int H, int I,
+                          int renormalize, void* out, void* router_logits, float* topk_weights, int32_t* topk_ids,
+                          void* ws, size_t ws_bytes, smb_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  GateIn gate;
+  gate.weight = gate_weight;
+  gate.logits_out = router_logits;
+  if (gate_weight == nullptr && T > 0) return SMB_ERR_NULL;
+  int rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize, topk_weights,
+                    topk_ids, ws, ws_bytes, s, EpLayout(), &gate);
   if (rc != SMB_OK) return rc;
   rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;

@@ -74,6 +74,21 @@ struct RouteArgs {
   int ep_G, ep_C, ep_Eloc;
 };
 
+// Router gate fused with the routing (gate_route_kernel): logits = x W^T of
+// ReplicatedLinear(H, E, bias=False) (specmoe/models/mixtral.py:85-92,111).
+struct GateArgs {
+  const void* x;        // [T, H] storage dtype
+  const void* weight;   // [E, H] storage dtype
+  float* logits;        // [T, E] workspace copy (values rounded to the storage dtype)
+  void* logits_out;     // optional [T, E] storage dtype
+  int* ticket;          // CTA ticket, 0 between launches
+  int T, E, H;
+  int route;            // 1: the last CTA routes all tokens with RouteArgs
+};
+
+cudaError_t launch_gate_route(const RouteArgs& a, const GateArgs& g, int dtype, int grid, cudaStream_t stream,
+                              bool pdl);
+
 cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int k, int renorm, float* out_w,
                         int32_t* out_ids, cudaStream_t stream);
 cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStream_t stream, bool pdl);

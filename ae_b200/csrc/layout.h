@@ -10,6 +10,7 @@ constexpr int kMaxExperts = 256;   // router keeps up to 8 logits per lane
 constexpr int kMaxTopK = 8;
 constexpr int kMaxFlat = 16384;    // T*k limit of the single-pass permutation
 constexpr size_t kAlign = 256;
+constexpr size_t kWsHeaderBytes = 256;  // status block at offset 0, zeroed by smb_moe_workspace_init
 
 // Status codes written to the device status word (first error wins).
 enum DeviceStatus : int {
@@ -24,8 +25,9 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Device scratch for one layer call.  Every buffer is owned by the caller (one
 // contiguous allocation); the library only carves it.
 struct WsLayout {
+  size_t status;      // int32 [64]    [0] device status word, [1] CTA ticket of the gated router;
+                      //               always at offset 0 so a buffer reused for other shapes keeps it
   size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert
-  size_t status;      // int32 [8]     device status word(s)
   size_t done;        // int32 [E*S+2] finished gate/up units per (expert, down split), then the FFN work
                       //               counter and the count of CTAs done gathering xp
   size_t xp;          // elem  [rows, H] token rows in expert-major order (gathered by the FFN kernel)
@@ -33,6 +35,7 @@ struct WsLayout {
   size_t inv;         // int32 [Tk]    inv[f] = p
   size_t w;           // fp32  [Tk]    routing weight of flat slot f
   size_t ids;         // int32 [Tk]    expert of flat slot f
+  size_t logits;      // fp32  [T, E]  router logits of the gated launch (rounded to the storage dtype)
   size_t a2;          // elem  [rows, I] silu(x W1^T) * (x W3^T) in expert-major order
   size_t part;        // fp32  [S, Tk, H] split-K partials of the down projection
   size_t total;
@@ -46,13 +49,14 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   L.rows = static_cast<int>(align_up(Tk, 64) + 64);
   L.splits = splits;
   size_t o = 0;
+  L.status = o;     o = align_up(o + sizeof(int32_t) * 64, kAlign);
   L.expert_off = o; o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
-  L.status = o;     o = align_up(o + sizeof(int32_t) * 8, kAlign);
   L.done = o;       o = align_up(o + sizeof(int32_t) * (static_cast<size_t>(E) * splits + 2), kAlign);
   L.perm = o;       o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.inv = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
   L.w = o;          o = align_up(o + sizeof(float) * Tk, kAlign);
   L.ids = o;        o = align_up(o + sizeof(int32_t) * Tk, kAlign);
+  L.logits = o;     o = align_up(o + sizeof(float) * static_cast<size_t>(T) * E, kAlign);
   L.xp = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * H, kAlign);
   L.a2 = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * I, kAlign);
   L.part = o;       o = align_up(o + sizeof(float) * static_cast<size_t>(splits) * Tk * H, kAlign);

@@ -28,9 +28,11 @@ constexpr int kRouteThreads = 512;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
 
+// L2 loads (ld.global.cg): in the gated launch the logits were written by other CTAs of
+// the same grid, so the SM's L1 must not serve them.
 template <typename TL>
 __device__ __forceinline__ float logit_at(const void* base, size_t idx) {
-  return to_f32<TL>(reinterpret_cast<const TL*>(base)[idx]);
+  return to_f32<TL>(__ldcg(reinterpret_cast<const TL*>(base) + idx));
 }
 
 // Top-k of one token's logits by a group of G lanes (G a power of two, G * 8 >= E):
@@ -142,9 +144,11 @@ __device__ __forceinline__ void route_dispatch(const void* logits, int t_begin, 
   }
 }
 
+// Routing + permutation of every flat slot by one CTA's worth of threads.  `cta` is the
+// index of the calling CTA among `ncta` that run the body redundantly (each writes the
+// outputs of its own flat range; CTA 0 also the offsets, headers and counters).
 template <typename TL>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a, int vec_per_row) {
-  extern __shared__ int32_t sm[];
+__device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, int cta, int32_t* sm) {
   const int Tk = a.T * a.k;
   const int E = a.E;
   int32_t* s_ids = sm;                                   // [Tk]
@@ -158,11 +162,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  pdl_wait_prior_grids();
-  pdl_launch_dependents();
   if (tid == 0) {
     s_bad = 0;
-    if (blockIdx.x == 0 && a.status != nullptr) a.status[0] = 0;
+    if (cta == 0 && a.status != nullptr) a.status[0] = 0;
   }
   __syncthreads();
 
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   }
   for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] = 0;
   __syncthreads();
-  if (tid == 0 && s_bad && blockIdx.x == 0) record_status(a.status, kDevBadExpertId);
+  if (tid == 0 && s_bad && cta == 0) record_status(a.status, kDevBadExpertId);
 
   // 2. per-warp histograms over contiguous flat segments
   const int seg = (Tk + kRouteWarps - 1) / kRouteWarps;
@@ -276,7 +278,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   __syncthreads();
 
   // 5. outputs for this CTA's flat range
-  if (blockIdx.x == 0) {
+  if (cta == 0) {
     for (int e = tid; e <= E; e += kRouteThreads) a.expert_off[e] = s_off[e];
     if (a.ep_send != nullptr) {
       // header row of each destination chunk: counts of that destination's experts
@@ -292,7 +294,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
       for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
     }
   }
-  const int g0 = min(Tk, static_cast<int>(blockIdx.x) * a.rows_per_cta);
+  const int g0 = min(Tk, cta * a.rows_per_cta);
   const int g1 = min(Tk, g0 + a.rows_per_cta);
   for (int f = g0 + tid; f < g1; f += kRouteThreads) {
     const int p = s_pos[f];
@@ -342,6 +344,127 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a,
   }
 }
 
+template <typename TL>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a, int vec_per_row) {
+  extern __shared__ int32_t sm[];
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  route_body<TL>(a, vec_per_row, static_cast<int>(blockIdx.x), sm);
+}
+
+// ---------------------------------------------------------------------------- gate
+
+// The 16 / sizeof(TX) elements of a 16-byte vector as fp32.
+template <typename TX>
+__device__ __forceinline__ void unpack16(const uint4& va, float (&f)[16 / sizeof(TX)]) {
+  const TX* v = reinterpret_cast<const TX*>(&va);
+#pragma unroll
+  for (int i = 0; i < static_cast<int>(16 / sizeof(TX)); ++i) f[i] = to_f32<TX>(v[i]);
+}
+
+constexpr int kGateTok = 2;   // tokens per CTA pass
+constexpr int kGateExp = 8;   // experts per pass
+
+// Router gate: logits[t, e] = sum_h x[t, h] * W[e, h] (ReplicatedLinear(H, E, bias=False),
+// specmoe/models/mixtral.py:85-92,111), fp32 accumulation, rounded once to the storage
+// dtype like the reference's half-precision linear output.  A CTA takes a contiguous
+// range of tokens, 2 tokens x 8 experts per pass; its 512 threads split H into 16-byte
+// vectors (each converted to fp32 once), each warp reduces its 16 values with a
+// 16-shuffle transpose-reduction, and 16 threads add the 16 warp sums in warp order, so
+// the result does not depend on timing.  With g.route set, every CTA then
+// takes a ticket and the last one to finish routes all tokens (route_body), reading the
+// logits the others wrote; it leaves the ticket at 0 for the next call.
+template <typename TX>
+__global__ void __launch_bounds__(kRouteThreads) gate_route_kernel(const RouteArgs a, const GateArgs g,
+                                                                   int vec_per_row) {
+  extern __shared__ int32_t sm[];
+  __shared__ float s_red[kRouteWarps][kGateTok * kGateExp];
+  __shared__ int s_last;
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int vpr = g.H * static_cast<int>(sizeof(TX)) / 16;
+  const uint4* xv = reinterpret_cast<const uint4*>(g.x);
+  const uint4* wv = reinterpret_cast<const uint4*>(g.weight);
+  // this CTA's tokens: a contiguous range, at most kGateTok per pass
+  const int per_cta = (g.T + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int t_begin = min(g.T, static_cast<int>(blockIdx.x) * per_cta);
+  const int t_end = min(g.T, t_begin + per_cta);
+  constexpr int kEl = 16 / static_cast<int>(sizeof(TX));
+  for (int t0 = t_begin; t0 < t_end; t0 += kGateTok) {
+    const int nt = min(kGateTok, t_end - t0);
+    for (int e0 = 0; e0 < g.E; e0 += kGateExp) {
+      float v[kGateTok * kGateExp];
+#pragma unroll
+      for (int i = 0; i < kGateTok * kGateExp; ++i) v[i] = 0.f;
+      for (int c = tid; c < vpr; c += kRouteThreads) {
+        float xf[kGateTok][kEl];
+#pragma unroll
+        for (int j = 0; j < kGateTok; ++j) {
+          uint4 xr = make_uint4(0u, 0u, 0u, 0u);
+          if (j < nt) xr = __ldg(xv + static_cast<size_t>(t0 + j) * vpr + c);
+          unpack16<TX>(xr, xf[j]);
+        }
+#pragma unroll
+        for (int e = 0; e < kGateExp; ++e) {
+          if (e0 + e < g.E) {
+            float wf[kEl];
+            unpack16<TX>(__ldg(wv + static_cast<size_t>(e0 + e) * vpr + c), wf);
+#pragma unroll
+            for (int j = 0; j < kGateTok; ++j) {
+              float acc = v[j * kGateExp + e];
+#pragma unroll
+              for (int i = 0; i < kEl; ++i) acc = fmaf(xf[j][i], wf[i], acc);
+              v[j * kGateExp + e] = acc;
+            }
+          }
+        }
+      }
+      // transpose-reduction of the NV = 16 values over the warp: after the step of width
+      // o, a lane holds o partial sums, of the half of the indices selected by its bit o;
+      // then lanes that differ only in bit 4 add their sums, and lane l holds value l % 16
+      constexpr int kNV = kGateTok * kGateExp;
+      static_assert(kNV == 16, "reduction below is written for 16 values");
+#pragma unroll
+      for (int o = kNV / 2; o >= 1; o >>= 1) {
+        const bool hi = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+          const float send = hi ? v[i] : v[i + o];
+          const float keep = hi ? v[i + o] : v[i];
+          v[i] = keep + __shfl_xor_sync(kFull, send, o);
+        }
+      }
+      v[0] += __shfl_xor_sync(kFull, v[0], 16);
+      if (lane < kNV) s_red[warp][lane] = v[0];
+      __syncthreads();
+      if (tid < kGateTok * kGateExp) {
+        const int j = tid / kGateExp, e = tid % kGateExp;
+        float s = 0.f;
+        for (int w = 0; w < kRouteWarps; ++w) s += s_red[w][tid];
+        if (j < nt && e0 + e < g.E) {
+          const TX r = from_f32<TX>(s);
+          const size_t o = static_cast<size_t>(t0 + j) * g.E + e0 + e;
+          if (g.logits != nullptr) g.logits[o] = to_f32<TX>(r);
+          if (g.logits_out != nullptr) reinterpret_cast<TX*>(g.logits_out)[o] = r;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (!g.route) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(g.ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) *g.ticket = 0;
+  route_body<float>(a, vec_per_row, 0, sm);
+}
+
 // Routing only (select_experts): one warp per token.
 template <typename TL>
 __global__ void __launch_bounds__(256) topk_kernel(const void* logits, int T, int E, int k, int renorm,
@@ -389,7 +512,7 @@ cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStrea
     default: fn = reinterpret_cast<const void*>(&route_kernel<float>); which = 2; break;
   }
   const size_t smem = route_smem_bytes(a.T, a.E, a.k);
-  cudaError_t err = smem > 48 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[which], 64) : cudaSuccess;
+  cudaError_t err = smem > 40 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[which], 64) : cudaSuccess;
   if (err != cudaSuccess) return err;
   int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * elem_bytes / 16);
   cudaLaunchConfig_t cfg = {};
@@ -403,6 +526,31 @@ cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStrea
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<RouteArgs*>(&a), &vec_per_row};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+cudaError_t launch_gate_route(const RouteArgs& a, const GateArgs& g, int dtype, int grid, cudaStream_t stream,
+                              bool pdl) {
+  static std::atomic<int> seen[2][64];
+  const bool bf16 = dtype == SMB_DTYPE_BF16;
+  const void* fn = bf16 ? reinterpret_cast<const void*>(&gate_route_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&gate_route_kernel<__half>);
+  const size_t smem = g.route ? route_smem_bytes(a.T, a.E, a.k) : 0;
+  cudaError_t err = smem > 40 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[bf16 ? 1 : 0], 64)
+                                     : cudaSuccess;
+  if (err != cudaSuccess) return err;
+  int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * 2 / 16);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<RouteArgs*>(&a), const_cast<GateArgs*>(&g), &vec_per_row};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

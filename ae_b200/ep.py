@@ -46,7 +46,8 @@ class CudaBackend:
         b = self._bufs.get(key)
         if b is None:
             if nbytes is not None:
-                b = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=self.device)
+                from . import ops
+                b = ops.new_workspace(nbytes, self.device)
             else:
                 b = torch.empty(*shape, dtype=dtype, device=self.device)
             self._bufs[key] = b

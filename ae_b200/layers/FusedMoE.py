@@ -47,6 +47,18 @@ def _make_pinned(nbytes: int, dtype: torch.dtype) -> torch.Tensor:
     return torch.empty(nbytes // elem, dtype=dtype, pin_memory=True)
 
 
+def expert_pool(layer: torch.nn.Module) -> torch.Tensor:
+    """The GPU page pool of a FusedMoE: ``ws.gpu_cache`` as linked by the engine
+    (``specmoe/models/mixtral.py:554-557``), or ``ws`` itself when it lives on the GPU."""
+    pool = getattr(layer.ws, "gpu_cache", None)
+    if pool is None:
+        if not layer.ws.is_cuda:
+            raise RuntimeError("FusedMoE.ws has no gpu_cache: the engine links the GPU expert pool "
+                               "(MixtralForCausalLMOff.link_gpu_experts_cache) before forward")
+        pool = layer.ws.data
+    return pool
+
+
 class UnquantizedFusedMoEMethod:
     """Weights and forward of the unquantised MoE (``FusedMoE.py:65-240``)."""
 
@@ -88,12 +100,7 @@ class UnquantizedFusedMoEMethod:
             raise NotImplementedError("apply_router_weight_on_input / no_combine")
         if routed_scaling_factor is not None:
             raise NotImplementedError("routed_scaling_factor")
-        pool = getattr(layer.ws, "gpu_cache", None)
-        if pool is None:
-            if not layer.ws.is_cuda:
-                raise RuntimeError("FusedMoE.ws has no gpu_cache: the engine links the GPU expert pool "
-                                   "(MixtralForCausalLMOff.link_gpu_experts_cache) before forward")
-            pool = layer.ws.data
+        pool = expert_pool(layer)
         # routing, permutation, expert FFN and combine; written in place like the
         # reference (stack_fused_moe(..., inplace=True), FusedMoE.py:187-196)
         return ops.moe_forward(x, router_logits.contiguous(), pool, expert_cache_indices, top_k,

@@ -61,7 +61,7 @@ class Workspace:
         with cls._lock:
             buf = cls._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
-                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                buf = new_workspace(max(nbytes, 1 << 20), device)
                 cls._bufs[key] = buf
             return buf
 
@@ -69,6 +69,13 @@ class Workspace:
     def clear(cls):
         with cls._lock:
             cls._bufs.clear()
+
+
+def new_workspace(nbytes: int, device) -> torch.Tensor:
+    """A workspace buffer with its control block initialised (``smb_moe_workspace_init``)."""
+    buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    _native.call("smb_moe_workspace_init", buf.data_ptr(), buf.numel(), _stream_ptr(buf.device))
+    return buf
 
 
 def workspace_bytes(T: int, E: int, k: int, H: int, I: int, dtype: torch.dtype) -> int:
@@ -162,6 +169,57 @@ def moe_forward_routed(x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: to
     return out
 
 
+def gate(x: torch.Tensor, gate_weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Router logits [T, E] = x [T, H] @ gate_weight [E, H]^T in the storage dtype
+    (``MixtralMoE.gate``, specmoe/models/mixtral.py:85-92)."""
+    _need_cuda("hidden_states", x)
+    _need_cuda("gate weight", gate_weight)
+    T, H = x.shape
+    E = gate_weight.shape[0]
+    if gate_weight.shape[1] != H or gate_weight.dtype != x.dtype:
+        raise ValueError("gate weight must be [E, H] in the dtype of hidden_states")
+    if out is None:
+        out = torch.empty(T, E, dtype=x.dtype, device=x.device)
+    _native.call("smb_moe_gate", x.data_ptr(), gate_weight.data_ptr(), storage_code(x.dtype), T, E, H,
+                 out.data_ptr(), _stream_ptr(x.device))
+    return out
+
+
+def moe_forward_gated(x: torch.Tensor, gate_weight: torch.Tensor, pool: torch.Tensor,
+                      page_of_expert: torch.Tensor, top_k: int, renormalize: bool = True,
+                      out: torch.Tensor | None = None, router_logits: torch.Tensor | None = None,
+                      topk_weights: torch.Tensor | None = None,
+                      topk_ids: torch.Tensor | None = None) -> torch.Tensor:
+    """MixtralMoE block (gate + experts, specmoe/models/mixtral.py:106-115 without the
+    TP all-reduce): the gate GEMV and the routing in one launch, then FFN and combine.
+    ``out`` may be ``x``.  Optional outputs: ``router_logits`` [T, E] (storage dtype),
+    ``topk_weights`` fp32 / ``topk_ids`` int32 [T, k]."""
+    for n, t in (("hidden_states", x), ("gate weight", gate_weight), ("expert pool", pool),
+                 ("expert_cache_indices", page_of_expert)):
+        _need_cuda(n, t)
+    T, H = x.shape
+    E = gate_weight.shape[0]
+    if gate_weight.shape[1] != H or gate_weight.dtype != x.dtype:
+        raise ValueError("gate weight must be [E, H] in the dtype of hidden_states")
+    if page_of_expert.dtype != torch.int64 or page_of_expert.numel() != E:
+        raise ValueError("expert_cache_indices must be int64 [E]")
+    if pool.dtype != x.dtype:
+        raise ValueError("expert pool and hidden_states dtypes differ")
+    P, I = pool_geometry(pool, H)
+    code = storage_code(x.dtype)
+    if out is None:
+        out = torch.empty_like(x)
+    nbytes = workspace_bytes(T, E, top_k, H, I, x.dtype)
+    ws = Workspace.get(x.device, nbytes)
+    stream = _stream_ptr(x.device)
+    _native.call("smb_moe_forward_gated", x.data_ptr(), gate_weight.data_ptr(), pool.data_ptr(), P,
+                 page_of_expert.data_ptr(), code, T, E, top_k, H, I, int(bool(renormalize)), out.data_ptr(),
+                 _ptr(router_logits), _ptr(topk_weights), _ptr(topk_ids), ws.data_ptr(), ws.numel(), stream)
+    if DEBUG:
+        _native.check("smb_moe_forward_gated (device status)", _status(ws, T, E, top_k, H, I, code, stream))
+    return out
+
+
 def topk(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
     """(topk_weights fp32 [T,k], topk_ids int32 [T,k]) on the GPU."""
     _need_cuda("router_logits", router_logits)
@@ -197,7 +255,7 @@ class StagedLayer:
         self.dtype = dtype
         self.code = storage_code(dtype)
         self.nbytes = workspace_bytes(T, E, k, H, I, dtype)
-        self.ws = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.ws = new_workspace(self.nbytes, device)
         self.device = torch.device(device)
 
     def _s(self):
@@ -248,12 +306,15 @@ class StagedLayer:
         S = splits(E, H, I, Tk)
         o = 0
         off = {}
-        for name, nb in (("expert_off", 4 * (E + 1)), ("status", 32), ("done", 4 * (E * S + 2)), ("perm", 4 * Tk),
-                         ("inv", 4 * Tk),
-                         ("w", 4 * Tk), ("ids", 4 * Tk), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
+        # mirrors ae_b200/csrc/layout.h::make_ws_layout (checked against its total below)
+        for name, nb in (("status", 4 * 64), ("expert_off", 4 * (E + 1)), ("done", 4 * (E * S + 2)),
+                         ("perm", 4 * Tk), ("inv", 4 * Tk), ("w", 4 * Tk), ("ids", 4 * Tk),
+                         ("logits", 4 * self.T * E), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
                          ("part", 4 * S * Tk * H)):
             off[name] = (o, nb)
             o = up(o + nb)
+        if o != self.nbytes:
+            raise RuntimeError(f"workspace layout mirror out of date ({o} != {self.nbytes} bytes)")
         ws = self.ws
 
         def view(name, dtype, shape):
@@ -262,12 +323,13 @@ class StagedLayer:
 
         return {
             "expert_off": view("expert_off", torch.int32, (E + 1,)),
-            "status": view("status", torch.int32, (8,)),
+            "status": view("status", torch.int32, (64,)),
             "done": view("done", torch.int32, (E * S + 2,)),
             "perm": view("perm", torch.int32, (Tk,)),
             "inv": view("inv", torch.int32, (Tk,)),
             "w": view("w", torch.float32, (Tk,)),
             "ids": view("ids", torch.int32, (Tk,)),
+            "logits": view("logits", torch.float32, (self.T, E)),
             "xp": view("xp", self.dtype, (rows, H)),
             "a2": view("a2", self.dtype, (rows, I)),
             "part": view("part", torch.float32, (S, Tk, H)),

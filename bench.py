@@ -384,6 +384,34 @@ def run_ours(args, cfg, rank, world, dev):
                                    configs.MoEConfig(cfg.name, cfg.H, cfg.I, cfg.E, cfg.k, Ts, cfg.router_std),
                                    cfg.E, Ts * cfg.k, splits)[1] / (el_s / n) / 1e9 / hbm_peak, 4)}
 
+    # the whole MixtralMoE block (gate + experts): gate fused into the routing launch vs.
+    # the reference's arrangement of a separate half-precision gate GEMM (cuBLAS, like
+    # ReplicatedLinear) followed by the layer
+    gated = None
+    if world == 1 and not args.no_sweep:
+        xg, wg = configs.make_gate_inputs(cfg, dev, seed=2)
+        og = torch.empty_like(xg)
+
+        def fused():
+            ops.moe_forward_gated(xg, wg, pool, pages, cfg.k, cfg.renormalize, out=og)
+
+        def unfused():
+            lg = torch.matmul(xg, wg.t())
+            ops.moe_forward(xg, lg, pool, pages, cfg.k, cfg.renormalize, out=og)
+
+        gated = {"api": "ae_b200.layers.mixtral_moe.MixtralMoE.forward (smb_moe_forward_gated)"}
+        for name, fn in (("fused_gate", fused), ("separate_gate_gemm", unfused)):
+            for _ in range(5):
+                fn()
+            gg = graph_of(fn, dev)
+            for _ in range(3):
+                gg.replay()
+            torch.cuda.synchronize(dev)
+            n = max(10, args.steps // 2)
+            el_g = timed_steps(gg.replay, n, stream)
+            gated[f"{name}_us_per_layer"] = round(el_g / n * 1e6, 2)
+            del gg
+
     # CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -438,6 +466,7 @@ def run_ours(args, cfg, rank, world, dev):
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
         "sweep": sweep,
+        "gated_block": gated,
     }
     print(json.dumps(line), flush=True)
 

@@ -175,6 +175,27 @@ SMB_API int smb_moe_forward_routed(const void* x, const float* topk_weights, con
                            int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H,
                            int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream);
 
+/* Zero the workspace's control block (its first 256 bytes).  Call once after allocating
+ * a workspace, before its first smb_moe_forward_gated call: the gated launch counts its
+ * CTAs in a ticket kept there, and every call leaves the ticket at 0 again. */
+SMB_API int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream);
+
+/* Router gate only: router_logits [T,E] = x [T,H] gate_weight[E,H]^T, fp32 accumulation,
+ * rounded to the storage dtype.  Replaces MixtralMoE.gate, a ReplicatedLinear(H, E,
+ * bias=False) in the storage dtype (specmoe/models/mixtral.py:85-92, called at :111). */
+SMB_API int smb_moe_gate(const void* x, const void* gate_weight, int dtype, int T, int E, int H, void* router_logits,
+                         smb_stream_t stream);
+
+/* Whole MixtralMoE block without the tensor-parallel all-reduce
+ * (specmoe/models/mixtral.py:106-115): the gate of smb_moe_gate and the routing run in
+ * one launch (router_logits, topk_weights, topk_ids: optional outputs, may be NULL),
+ * then the FFN and the combine as smb_moe_forward.  The workspace must have been
+ * initialised once with smb_moe_workspace_init. */
+SMB_API int smb_moe_forward_gated(const void* x, const void* gate_weight, const void* pool, int64_t num_pages,
+                                  const int64_t* page_of_expert, int dtype, int T, int E, int k, int H, int I,
+                                  int renormalize, void* out, void* router_logits, float* topk_weights,
+                                  int32_t* topk_ids, void* ws, size_t ws_bytes, smb_stream_t stream);
+
 /* smb_moe_forward without any device allocation, for callers that cannot allocate
  * device memory at call time (a host whose allocator owns the HBM, a latency-critical
  * path where cudaMalloc's implicit synchronisation is not allowed, a binding without a

@@ -226,6 +226,27 @@ def fused_moe_forward(hidden_states, router_logits, pool, page_of_expert, top_k:
     return out, w, ids
 
 
+def gate_logits(hidden_states, gate_weight):
+    """Router logits of ``MixtralMoE.gate`` (``specmoe/models/mixtral.py:85-92``, called at
+    ``:111``): ``ReplicatedLinear(H, E, bias=False)`` in the params dtype, i.e.
+    ``x @ W^T`` accumulated in high precision (fp64 here) and rounded once to the storage
+    dtype of ``hidden_states``.  Returns the logits in that dtype."""
+    x = torch.as_tensor(hidden_states)
+    w = torch.as_tensor(gate_weight)
+    return (x.double() @ w.double().t()).to(x.dtype)
+
+
+def mixtral_moe_forward(hidden_states, gate_weight, pool, page_of_expert, top_k: int,
+                        rounding: str = "fp32"):
+    """``MixtralMoE.forward`` (``specmoe/models/mixtral.py:106-115``) without the TP
+    all-reduce: the gate, then ``FusedMoE.forward`` with ``renormalize=True`` (``:99``).
+    Returns ``(out, router_logits, topk_weights, topk_ids)``."""
+    logits = gate_logits(hidden_states, gate_weight)
+    out, w, ids = fused_moe_forward(hidden_states, logits.float(), pool, page_of_expert, top_k, True,
+                                    rounding=rounding)
+    return out, logits, w, ids
+
+
 def error_metrics(got, ref):
     """(max-abs error, relative-L2 error) of ``got`` against the fp32 ``ref``."""
     g = torch.as_tensor(got).double()

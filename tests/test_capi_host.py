@@ -45,6 +45,12 @@ def test_argument_checks_without_gpu(lib):
     assert lib.smb_moe_topk(None, 1, 1, 8, 9, 1, None, None, None) == -1
     assert lib.smb_moe_topk(None, 1, 0, 8, 2, 1, None, None, None) == 0  # T = 0: nothing to do
     assert lib.smb_moe_splits(8, 100, 3584, 64) == -1
+    assert lib.smb_moe_gate(None, None, 7, 4, 8, 1024, None, None) == -2
+    assert lib.smb_moe_gate(None, None, 1, 4, 8, 100, None, None) == -1
+    assert lib.smb_moe_gate(None, None, 1, 4, 257, 1024, None, None) == -1
+    assert lib.smb_moe_gate(None, None, 1, 0, 8, 1024, None, None) == 0   # T = 0: nothing to do
+    assert lib.smb_moe_workspace_init(None, 1 << 20, None) == -8
+    assert lib.smb_moe_workspace_init(16, 1 << 20, None) == -3            # not 256-byte aligned
 
 
 def test_no_host_fallback_in_product_path():

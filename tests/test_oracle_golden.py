@@ -88,3 +88,16 @@ def test_permutation_is_stable_and_complete():
         seg = perm[off[e]:off[e + 1]]
         assert (flat[seg] == e).all()
         assert (np.diff(seg) > 0).all()
+
+
+def test_gate_logits_oracle_rounds_once():
+    """The gate restatement rounds the exact dot products once to the storage dtype."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(6, 256, generator=g).to(torch.bfloat16)
+    w = (torch.randn(8, 256, generator=g) * 0.05).to(torch.bfloat16)
+    got = mo.gate_logits(x, w)
+    assert got.dtype == torch.bfloat16 and got.shape == (6, 8)
+    exact = x.double() @ w.double().t()
+    assert torch.equal(got, exact.to(torch.bfloat16))
+    # fp32 accumulation in another order differs from the exact sum by far less than a bf16 ulp
+    assert float((exact - (x.float() @ w.float().t()).double()).abs().max()) < 1e-4
