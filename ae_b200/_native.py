@@ -38,6 +38,8 @@ SIGNATURES = {
     "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_noalloc": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "smb_moe_forward_shared": (_I, [_P, _P, _I, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P,
+                                    _S, _P]),
     "smb_moe_workspace_init": (_I, [_P, _S, _P]),
     "smb_moe_gate": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "smb_moe_forward_gated": (_I, [_P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _S, _P]),

@@ -75,9 +75,12 @@ def make_inputs(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, T: 
     wr = torch.randn(cfg.E, cfg.H, generator=g, device=device, dtype=torch.float32) * cfg.router_std
     logits = x @ wr.t()
     if cfg.zipf_s > 0:
-        # bias so that softmax popularity follows (rank+1)^-s over a seeded rank order
+        # expert popularity ~ Zipf(s) over a seeded rank order: bias -s*log(rank+1) plus
+        # Gumbel(0,1) noise per (token, expert), so the top-1 choice is expert e with
+        # probability (rank_e+1)^-s / sum (Gumbel-max) and the top-k choices follow it
         ranks = torch.randperm(cfg.E, generator=g, device=device).float()
-        logits = logits + (-cfg.zipf_s * torch.log(ranks + 1.0)).unsqueeze(0)
+        u = torch.rand(T, cfg.E, generator=g, device=device).clamp_(1e-12, 1.0 - 1e-7)
+        logits = logits + (-cfg.zipf_s * torch.log(ranks + 1.0)).unsqueeze(0) - torch.log(-torch.log(u))
     return x.to(dtype), logits.to(dtype)
 
 

@@ -216,9 +216,17 @@ struct GateIn {
   void* logits_out = nullptr;    // optional [T, E] storage dtype
 };
 
+// Shared expert as n pseudo-experts (the last n of E) that every token takes.
+struct SharedIn {
+  int n = 0;
+  const float* w = nullptr;  // [T] or nullptr (weight 1)
+};
+
+// E and k count the shared pseudo-experts / slots too.
 int do_route(const void* logits, int logits_dtype, const float* in_w, const int32_t* in_ids, const void* x,
              int dtype, int T, int E, int k, int H, int I, int renorm, float* out_w, int32_t* out_ids, void* ws,
-             size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout(), const GateIn* gate = nullptr) {
+             size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout(), const GateIn* gate = nullptr,
+             const SharedIn& shared = SharedIn()) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
@@ -245,6 +253,9 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.T = T;
   a.E = E;
   a.k = k;
+  a.k_routed = k - shared.n;
+  a.n_shared = shared.n;
+  a.shared_w = shared.w;
   a.H = H;
   a.renormalize = renorm ? 1 : 0;
   a.out_w = out_w;
@@ -273,7 +284,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
     g.logits_out = gate->logits_out;
     g.ticket = at<int>(ws, L.status) + 1;
     g.T = T;
-    g.E = E;
+    g.E = E - shared.n;
     g.H = H;
     g.route = 1;
     a.logits = g.logits;
@@ -533,6 +544,25 @@ int smb_moe_forward_routed(const void* x, const float* topk_weights, const int32
   return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }
 
+int smb_moe_forward_shared(const void* x, const void* router_logits, int logits_dtype, const float* shared_weight,
+                           const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype, int T,
+                           int E, int k, int n_shared, int H, int I, int renormalize, void* out,
+                           float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (n_shared < 0 || k < 1 || k > E) return SMB_ERR_SHAPE;
+  if (router_logits == nullptr && T > 0) return SMB_ERR_NULL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SharedIn sh;
+  sh.n = n_shared;
+  sh.w = shared_weight;
+  const int Et = E + n_shared, kt = k + n_shared;
+  int rc = do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, Et, kt, H, I, renormalize,
+                    topk_weights, topk_ids, ws, ws_bytes, s, EpLayout(), nullptr, sh);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, Et, kt, H, I, ws, ws_bytes, s, 3, true);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out, dtype, T, Et, kt, H, I, ws, ws_bytes, s);
+}
+
 int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream) {
   if (ws == nullptr) return SMB_ERR_NULL;
   if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
@@ -556,6 +586,7 @@ int smb_moe_gate(const void* x, const void* gate_weight, int dtype, int T, int E
   a.T = T;
   a.E = E;
   a.k = 1;
+  a.k_routed = 1;
   a.H = H;
   GateArgs g{};
   g.x = x;

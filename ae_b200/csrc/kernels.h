@@ -55,7 +55,10 @@ struct RouteArgs {
   const float* in_w;       // [T, k] given routing weights (logits == nullptr)
   const int32_t* in_ids;   // [T, k] given expert ids
   const void* x;           // [T, H] token rows
-  int T, E, k, H, renormalize;
+  int T, E, k, H, renormalize;  // E, k: all experts / slots per token, shared ones included
+  int k_routed;            // top-k slots per token (k - n_shared)
+  int n_shared;            // pseudo-experts E-n_shared..E-1 every token takes (a shared expert)
+  const float* shared_w;   // [T] weight of the shared slots, or nullptr for 1
   float* out_w;            // optional [T, k]
   int32_t* out_ids;        // optional [T, k]
   int32_t* expert_off;     // workspace

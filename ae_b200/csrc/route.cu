@@ -103,8 +103,8 @@ __device__ __forceinline__ void route_token_group(const void* logits, int t, int
   }
 }
 
-// Route tokens [t_begin, t_end) with groups of G lanes over nthreads threads; writes
-// ids / weights of slot t*k+j through the callback.
+// Route tokens [t_begin, t_end) with groups of G lanes over nthreads threads; hands
+// (token t, choice j, expert id, weight) to the callback.
 template <typename TL, int G, typename Sink>
 __device__ __forceinline__ void route_range(const void* logits, int t_begin, int t_end, int E, int k, int renorm,
                                             int tid, int nthreads, Sink sink) {
@@ -120,7 +120,7 @@ __device__ __forceinline__ void route_range(const void* logits, int t_begin, int
     if (t < t_end) {
 #pragma unroll
       for (int j = 0; j < kMaxTopK; ++j) {
-        if (j < k && (j % G) == q) sink(t * k + j, ids[j], ws[j]);
+        if (j < k && (j % G) == q) sink(t, j, ids[j], ws[j]);
       }
     }
   }
@@ -170,10 +170,22 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
 
   // 1. routing of every token (or the given routing)
   if (a.logits != nullptr) {
-    route_dispatch<TL>(a.logits, 0, a.T, E, a.k, a.renormalize, tid, kRouteThreads, [&](int f, int id, float w) {
-      s_ids[f] = id;
-      s_w[f] = w;
-    });
+    // softmax / top-k over the routed experts, then the shared slots: every token also
+    // takes the n_shared pseudo-experts E_routed.. (pieces of one shared expert along its
+    // intermediate dimension) with the shared weight
+    const int Er = E - a.n_shared;
+    route_dispatch<TL>(a.logits, 0, a.T, Er, a.k_routed, a.renormalize, tid, kRouteThreads,
+                       [&](int t, int j, int id, float w) {
+                         const int f = t * a.k + j;
+                         s_ids[f] = id;
+                         s_w[f] = w;
+                       });
+    for (int i = tid; i < a.T * a.n_shared; i += kRouteThreads) {
+      const int t = i / a.n_shared, q = i - (i / a.n_shared) * a.n_shared;
+      const int f = t * a.k + a.k_routed + q;
+      s_ids[f] = Er + q;
+      s_w[f] = a.shared_w != nullptr ? a.shared_w[t] : 1.0f;
+    }
   } else if (a.ep_recv != nullptr) {
     // expert side of the exchange: payload row f = s*C + i of source s belongs to the
     // local expert whose run of the source's header counts holds i (k = 1, weight 1)
@@ -196,14 +208,22 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
       s_w[f] = 1.0f;
     }
   } else {
+    // given routing [T, k_routed] (+ the shared slots, as above)
+    const int Er = E - a.n_shared;
     for (int f = tid; f < Tk; f += kRouteThreads) {
-      int id = a.in_ids[f];
-      if (id != -1 && (id < 0 || id >= E)) {
-        s_bad = 1;
-        id = 0;
+      const int t = f / a.k, j = f - (f / a.k) * a.k;
+      if (j < a.k_routed) {
+        int id = a.in_ids[t * a.k_routed + j];
+        if (id != -1 && (id < 0 || id >= Er)) {
+          s_bad = 1;
+          id = 0;
+        }
+        s_ids[f] = id;  // -1: the slot has no expert (padding of the expert-parallel exchange)
+        s_w[f] = a.in_w[t * a.k_routed + j];
+      } else {
+        s_ids[f] = Er + (j - a.k_routed);
+        s_w[f] = a.shared_w != nullptr ? a.shared_w[t] : 1.0f;
       }
-      s_ids[f] = id;  // -1: the slot has no expert (padding of the expert-parallel exchange)
-      s_w[f] = a.in_w[f];
     }
   }
   for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] = 0;
@@ -302,8 +322,11 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     a.inv[f] = p;
     a.ws_w[f] = s_w[f];
     a.ws_ids[f] = s_ids[f];
-    if (a.out_w != nullptr) a.out_w[f] = s_w[f];
-    if (a.out_ids != nullptr) a.out_ids[f] = s_ids[f];
+    const int t = f / a.k, j = f - (f / a.k) * a.k;
+    if (j < a.k_routed) {  // the caller's routing outputs [T, k_routed] leave out the shared slots
+      if (a.out_w != nullptr) a.out_w[t * a.k_routed + j] = s_w[f];
+      if (a.out_ids != nullptr) a.out_ids[t * a.k_routed + j] = s_ids[f];
+    }
   }
   // expert-parallel dispatch: token rows of this CTA's flat range into the exchange
   // layout, all threads on all rows, four independent 16-byte loads in flight per thread
@@ -476,7 +499,8 @@ __global__ void __launch_bounds__(256) topk_kernel(const void* logits, int T, in
   const int t0 = blockIdx.x * per_cta;
   const int t1 = min(T, t0 + per_cta);
   if (t0 >= T) return;
-  route_dispatch<TL>(logits, t0, t1, E, k, renorm, threadIdx.x, blockDim.x, [&](int f, int id, float w) {
+  route_dispatch<TL>(logits, t0, t1, E, k, renorm, threadIdx.x, blockDim.x, [&](int t, int j, int id, float w) {
+    const int f = t * k + j;
     out_w[f] = w;
     out_ids[f] = id;
   });

@@ -140,6 +140,65 @@ def moe_forward(x: torch.Tensor, router_logits: torch.Tensor, pool: torch.Tensor
     return out
 
 
+def shared_expert_pages(w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, I: int) -> torch.Tensor:
+    """A shared expert (w1, w3 [I_s, H], w2 [H, I_s]) as ceil(I_s / I) pages of the routed
+    experts' page layout [w1 | w3 | w2] with intermediate size I: page q holds rows
+    [q*I, (q+1)*I) of w1 / w3 and those columns of w2, zero-padded past I_s.  Returns
+    [n_shared, 3*I*H] on the device of w1 (a load-time repacking, like weight_loader)."""
+    Is, H = w1.shape
+    if w3.shape != (Is, H) or w2.shape != (H, Is):
+        raise ValueError("shared expert weights must be w1, w3 [I_s, H] and w2 [H, I_s]")
+    n = -(-Is // I)
+    pages = torch.zeros(n, 3 * I * H, dtype=w1.dtype, device=w1.device)
+    for q in range(n):
+        r0, r1 = q * I, min(Is, (q + 1) * I)
+        p = pages[q]
+        p[: I * H].view(I, H)[: r1 - r0] = w1[r0:r1]
+        p[I * H: 2 * I * H].view(I, H)[: r1 - r0] = w3[r0:r1]
+        p[2 * I * H:].view(H, I)[:, : r1 - r0] = w2[:, r0:r1]
+    return pages
+
+
+def moe_forward_shared(x: torch.Tensor, router_logits: torch.Tensor, pool: torch.Tensor,
+                       page_of_expert: torch.Tensor, top_k: int, n_shared: int,
+                       shared_weight: torch.Tensor | None = None, renormalize: bool = True,
+                       out: torch.Tensor | None = None, topk_weights: torch.Tensor | None = None,
+                       topk_ids: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed top-k experts plus a shared expert (``n_shared`` pseudo-expert pages from
+    :func:`shared_expert_pages`, at ``page_of_expert[E:]``), scaled per token by
+    ``shared_weight`` fp32 [T] (None: 1).  ``router_logits`` [T, E] cover the routed experts."""
+    for n, t in (("hidden_states", x), ("router_logits", router_logits), ("expert pool", pool),
+                 ("page_of_expert", page_of_expert)):
+        _need_cuda(n, t)
+    T, H = x.shape
+    E = router_logits.shape[1]
+    if router_logits.shape[0] != T:
+        raise ValueError("Number of tokens mismatch")
+    if page_of_expert.dtype != torch.int64 or page_of_expert.numel() != E + n_shared:
+        raise ValueError("page_of_expert must be int64 [E + n_shared]")
+    if shared_weight is not None:
+        _need_cuda("shared_weight", shared_weight)
+        if shared_weight.dtype != torch.float32 or shared_weight.numel() != T:
+            raise ValueError("shared_weight must be float32 [T]")
+    if pool.dtype != x.dtype:
+        raise ValueError("expert pool and hidden_states dtypes differ")
+    P, I = pool_geometry(pool, H)
+    code = storage_code(x.dtype)
+    if out is None:
+        out = torch.empty_like(x)
+    nbytes = workspace_bytes(T, E + n_shared, top_k + n_shared, H, I, x.dtype)
+    ws = Workspace.get(x.device, nbytes)
+    stream = _stream_ptr(x.device)
+    _native.call("smb_moe_forward_shared", x.data_ptr(), router_logits.data_ptr(), logits_code(router_logits.dtype),
+                 _ptr(shared_weight), pool.data_ptr(), P, page_of_expert.data_ptr(), code, T, E, top_k, n_shared,
+                 H, I, int(bool(renormalize)), out.data_ptr(), _ptr(topk_weights), _ptr(topk_ids), ws.data_ptr(),
+                 ws.numel(), stream)
+    if DEBUG:
+        _native.check("smb_moe_forward_shared (device status)",
+                      _status(ws, T, E + n_shared, top_k + n_shared, H, I, code, stream))
+    return out
+
+
 def moe_forward_routed(x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                        pool: torch.Tensor, page_of_expert: torch.Tensor, num_experts: int,
                        out: torch.Tensor | None = None) -> torch.Tensor:

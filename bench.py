@@ -412,6 +412,12 @@ def run_ours(args, cfg, rank, world, dev):
             gated[f"{name}_us_per_layer"] = round(el_g / n * 1e6, 2)
             del gg
 
+    # the fine-grained configuration with a shared expert (60 routed experts of I 1408,
+    # top-4, shared expert I 5632 as 4 pseudo-experts in the same launch, Zipf routing)
+    fine = None
+    if world == 1 and not args.no_sweep:
+        fine = bench_shared_config(configs.BY_KEY["c3"], dev, stream, max(10, args.steps // 2), hbm_peak)
+
     # CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -467,8 +473,54 @@ def run_ours(args, cfg, rank, world, dev):
         "clocks": clocks,
         "sweep": sweep,
         "gated_block": gated,
+        "shared_expert_config": fine,
     }
     print(json.dumps(line), flush=True)
+
+
+def bench_shared_config(cfg, dev, stream, n, hbm_peak):
+    """Graph-replay time of one layer call of a shared-expert configuration (routed top-k
+    plus a sigmoid-gated shared expert), with its HBM roofline fraction."""
+    from ae_b200 import configs, ops
+    x, logits = configs.make_inputs(cfg, dev, seed=0)
+    routed = configs.make_pool(cfg, dev, seed=0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    H, Is = cfg.H, cfg.shared_I
+    w1 = (torch.randn(Is, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn(Is, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(H, Is, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wsg = (torch.randn(H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    shared = ops.shared_expert_pages(w1, w3, w2, cfg.I)
+    ns = shared.shape[0]
+    pool = torch.cat([routed, shared])
+    del routed, w1, w3, w2
+    pages = torch.arange(cfg.E + ns, device=dev, dtype=torch.int64)
+    out = torch.empty_like(x)
+    sw = torch.empty(cfg.T, dtype=torch.float32, device=dev)
+
+    def step():
+        torch.sigmoid(torch.matmul(x, wsg.unsqueeze(1)).squeeze(1).float(), out=sw)
+        ops.moe_forward_shared(x, logits, pool, pages, cfg.k, ns, sw, cfg.renormalize, out=out)
+
+    for _ in range(5):
+        step()
+    gr = graph_of(step, dev)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize(dev)
+    el = timed_steps(gr.replay, n, stream)
+    ids = torch.topk(logits.float(), cfg.k, dim=1).indices
+    touched = int((torch.bincount(ids.flatten(), minlength=cfg.E) > 0).sum())
+    alg = (touched * 3 * cfg.I * H + 3 * Is * H) * 2 + 2 * cfg.T * H * 2 + cfg.T * cfg.E * 2
+    us = el / n * 1e6
+    del gr
+    return {"workload": cfg.name + f" + shared expert I{Is} ({ns} pseudo-experts)", "T": cfg.T,
+            "us_per_layer": round(us, 2), "tokens_per_s": round(cfg.T / (el / n), 1),
+            "experts_touched": touched, "alg_bytes": alg,
+            "layer_hbm_frac": round(alg / (el / n) / 1e9 / hbm_peak, 4),
+            "api": "ae_b200.ops.moe_forward_shared (smb_moe_forward_shared)",
+            "note": "sigmoid shared gate (torch GEMV) + one library call per replay"}
 
 
 def run_ep(args, cfg, rank, world, dev):

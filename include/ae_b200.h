@@ -175,6 +175,23 @@ SMB_API int smb_moe_forward_routed(const void* x, const float* topk_weights, con
                            int64_t num_pages, const int64_t* page_of_expert, int dtype, int T, int E, int k, int H,
                            int I, void* out, void* ws, size_t ws_bytes, smb_stream_t stream);
 
+/* Layer with a shared expert (a Qwen2-MoE-style block: routed top-k experts plus one
+ * expert every token takes, scaled by shared_weight[t], e.g. sigmoid of a shared gate;
+ * NULL = 1).  The reference has no shared expert; this extends smb_moe_forward for the
+ * fine-grained configurations.  The shared expert of intermediate size I_s is passed as
+ * n_shared = ceil(I_s / I) pseudo-experts of intermediate I (SwiGLU is separable along
+ * the intermediate dimension): page q holds rows [q*I, (q+1)*I) of its w1 and w3 and the
+ * same columns of w2, zero-padded past I_s; their pages are page_of_expert[E ..
+ * E+n_shared-1].  The pseudo-experts share the grouped GEMM launch with the routed ones.
+ * router_logits [T, E] cover the routed experts; topk_weights / topk_ids [T, k] as in
+ * smb_moe_route; ws sized by smb_moe_workspace_bytes(T, E+n_shared, k+n_shared, H, I, dtype);
+ * k + n_shared <= 8. */
+SMB_API int smb_moe_forward_shared(const void* x, const void* router_logits, int logits_dtype,
+                                   const float* shared_weight, const void* pool, int64_t num_pages,
+                                   const int64_t* page_of_expert, int dtype, int T, int E, int k, int n_shared,
+                                   int H, int I, int renormalize, void* out, float* topk_weights, int32_t* topk_ids,
+                                   void* ws, size_t ws_bytes, smb_stream_t stream);
+
 /* Zero the workspace's control block (its first 256 bytes).  Call once after allocating
  * a workspace, before its first smb_moe_forward_gated call: the gated launch counts its
  * CTAs in a ticket kept there, and every call leaves the ticket at 0 again. */

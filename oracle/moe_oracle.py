@@ -247,6 +247,21 @@ def mixtral_moe_forward(hidden_states, gate_weight, pool, page_of_expert, top_k:
     return out, logits, w, ids
 
 
+def shared_expert_forward(hidden_states, w1, w3, w2, shared_weight=None):
+    """A shared expert computed directly, in fp32: ``s_t * w2 (silu(w1 x_t) * (w3 x_t))``
+    with w1, w3 [I_s, H], w2 [H, I_s] and ``s_t = shared_weight[t]`` (1 when None).  The
+    reference (SpecMoE) has no shared expert; this states the Qwen2-MoE-style block the
+    fine-grained benchmark configuration names (shared expert output added to the routed
+    experts' sum, scaled by the sigmoid of a shared gate)."""
+    x = torch.as_tensor(hidden_states).float()
+    g = x @ torch.as_tensor(w1).float().t()
+    u = x @ torch.as_tensor(w3).float().t()
+    y = (torch.nn.functional.silu(g) * u) @ torch.as_tensor(w2).float().t()
+    if shared_weight is not None:
+        y = y * torch.as_tensor(shared_weight).float().view(-1, 1)
+    return y
+
+
 def error_metrics(got, ref):
     """(max-abs error, relative-L2 error) of ``got`` against the fp32 ``ref``."""
     g = torch.as_tensor(got).double()

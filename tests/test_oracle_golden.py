@@ -101,3 +101,24 @@ def test_gate_logits_oracle_rounds_once():
     assert torch.equal(got, exact.to(torch.bfloat16))
     # fp32 accumulation in another order differs from the exact sum by far less than a bf16 ulp
     assert float((exact - (x.float() @ w.float().t()).double()).abs().max()) < 1e-4
+
+
+@pytest.mark.parametrize("Is,I", [(320, 128), (256, 128), (64, 64), (5632, 1408)])
+def test_shared_expert_pages_split_is_exact(Is, I):
+    """A shared expert cut into ceil(Is/I) zero-padded pages of intermediate I gives the same
+    FFN as the whole expert (SwiGLU is separable along the intermediate dimension)."""
+    from ae_b200.ops import shared_expert_pages
+    H = 128
+    g = torch.Generator().manual_seed(Is)
+    w1 = torch.randn(Is, H, generator=g) * 0.05
+    w3 = torch.randn(Is, H, generator=g) * 0.05
+    w2 = torch.randn(H, Is, generator=g) * 0.05
+    x = torch.randn(9, H, generator=g)
+    pages = shared_expert_pages(w1, w3, w2, I)
+    assert pages.shape == (-(-Is // I), 3 * I * H)
+    direct = mo.shared_expert_forward(x, w1, w3, w2)
+    pieces = torch.zeros_like(direct)
+    for p in pages:
+        a, b, c = mo.page_views(p, H, I)
+        pieces += (torch.nn.functional.silu(x @ a.t()) * (x @ b.t())) @ c.t()
+    torch.testing.assert_close(pieces, direct, rtol=1e-4, atol=1e-5)
