@@ -399,24 +399,35 @@ def run_ours(args, cfg, rank, world, dev):
             lg = torch.matmul(xg, wg.t())
             ops.moe_forward(xg, lg, pool, pages, cfg.k, cfg.renormalize, out=og)
 
-        gated = {"api": "ae_b200.layers.mixtral_moe.MixtralMoE.forward (smb_moe_forward_gated)"}
+        gated = {"api": "ae_b200.layers.mixtral_moe.MixtralMoE.forward (smb_moe_forward_gated)",
+                 "timing": "graph replays, the two arrangements alternated 4 times, median"}
+        graphs = {}
         for name, fn in (("fused_gate", fused), ("separate_gate_gemm", unfused)):
             for _ in range(5):
                 fn()
-            gg = graph_of(fn, dev)
-            for _ in range(3):
-                gg.replay()
-            torch.cuda.synchronize(dev)
-            n = max(10, args.steps // 2)
-            el_g = timed_steps(gg.replay, n, stream)
-            gated[f"{name}_us_per_layer"] = round(el_g / n * 1e6, 2)
-            del gg
+            graphs[name] = graph_of(fn, dev)
+        samples = {name: [] for name in graphs}
+        n = max(10, args.steps // 4)
+        for _ in range(4):
+            for name, gg in graphs.items():
+                for _ in range(3):
+                    gg.replay()
+                samples[name].append(timed_steps(gg.replay, n, stream) / n * 1e6)
+        for name, v in samples.items():
+            gated[f"{name}_us_per_layer"] = round(statistics.median(v), 2)
+        del graphs
 
     # the fine-grained configuration with a shared expert (60 routed experts of I 1408,
     # top-4, shared expert I 5632 as 4 pseudo-experts in the same launch, Zipf routing)
     fine = None
     if world == 1 and not args.no_sweep:
         fine = bench_shared_config(configs.BY_KEY["c3"], dev, stream, max(10, args.steps // 2), hbm_peak)
+
+    # the 32-layer verify step (Mixtral-8x7B architecture, batch 4 x 32-token draft tree on
+    # a 2048-token KV cache), MoE layers isolated by CUDA events around each MoE call
+    verify = None
+    if world == 1 and not args.no_sweep and not args.no_verify:
+        verify = bench_verify_step(dev, stream, hbm_peak)
 
     # CPU baseline (rank 0, N = 1)
     cpu = None
@@ -474,6 +485,7 @@ def run_ours(args, cfg, rank, world, dev):
         "sweep": sweep,
         "gated_block": gated,
         "shared_expert_config": fine,
+        "verify_32_layers": verify,
     }
     print(json.dumps(line), flush=True)
 
@@ -521,6 +533,52 @@ def bench_shared_config(cfg, dev, stream, n, hbm_peak):
             "layer_hbm_frac": round(alg / (el / n) / 1e9 / hbm_peak, 4),
             "api": "ae_b200.ops.moe_forward_shared (smb_moe_forward_shared)",
             "note": "sigmoid shared gate (torch GEMV) + one library call per replay"}
+
+
+def bench_verify_step(dev, stream, hbm_peak, steps: int = 5):
+    """Verify step of a random-init 32-layer Mixtral-8x7B decoder (ae_b200/verify.py):
+    batch 4 x 32 draft tokens (a seeded tree) over a 2048-token bf16 KV cache, 128 tokens
+    per MoE layer.  Returns the MoE layers' device time (events around each call), the
+    whole step and the MoE share."""
+    from ae_b200.verify import MIXTRAL_8X7B, VerifyDecoder, accept_greedy, random_tree
+    cfg = MIXTRAL_8X7B
+    B, n, cache = 4, 32, 2048
+    dec = VerifyDecoder(cfg, batch=B, cache_len=cache, max_draft=n, device=dev, seed=0)
+    parents = random_tree(n, seed=0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    tokens = torch.randint(0, cfg.vocab, (B, n), generator=g, device=dev)
+    for _ in range(3):
+        dec.forward(tokens, parents)
+    torch.cuda.synchronize(dev)
+    moe_us, step_us = [], []
+    for _ in range(steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(cfg.layers)]
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        logits = dec.forward(tokens, parents, moe_events=ev)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        moe_us.append(statistics.mean(a.elapsed_time(b) for a, b in ev) * 1000.0)
+        step_us.append(s0.elapsed_time(s1) * 1000.0)
+    acc, n_acc = accept_greedy(logits, tokens, parents, logits[:, 0])
+    T = B * n
+    layer_bytes = cfg.E * 3 * cfg.H * cfg.I * 2 + 2 * T * cfg.H * 2
+    m = statistics.median(moe_us)
+    out = {"workload": "C4 Mixtral-8x7B 32-layer verify step: batch 4 x 32-token draft tree, 2048-token bf16 KV "
+                       "cache, random-init weights",
+           "tokens_per_moe_layer": T, "moe_us_per_layer": round(m, 2),
+           "moe_layer_hbm_frac": round(layer_bytes / (m * 1e-6) / 1e9 / hbm_peak, 4),
+           "step_ms": round(statistics.median(step_us) / 1000.0, 3),
+           "moe_share_of_step": round(m * cfg.layers / statistics.median(step_us), 4),
+           "api": "ae_b200.verify.VerifyDecoder (MoE: smb_moe_forward_gated per layer)",
+           "accepted_tokens_per_seq": n_acc.tolist(),
+           "note": "eager launches; attention is torch SDPA with a tree mask; MoE time from CUDA events around "
+                   "each MoE call, median over %d steps" % steps}
+    del dec
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_ep(args, cfg, rank, world, dev):
@@ -674,6 +732,7 @@ def main():
     ap.add_argument("--staged-steps", type=int, default=20)
     ap.add_argument("--sweep", type=int, nargs="*", default=[16, 64])
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-verify", action="store_true", help="skip the 32-layer verify-step block")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
