@@ -94,12 +94,36 @@ int check_shape(int T, int E, int k, int H, int I, int dtype) {
   return SMB_OK;
 }
 
+// choose_splits simulates the unit queue (a few ms for the largest shapes), so its
+// answer is kept per shape.
+int cached_splits(int E, int H, int I, int Tk, int sms) {
+  struct Entry {
+    int E, H, I, Tk, sms, s;
+  };
+  constexpr int kSlots = 128;
+  static Entry table[kSlots];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+      const Entry& t = table[i];
+      if (t.E == E && t.H == H && t.I == I && t.Tk == Tk && t.sms == sms) return t.s;
+    }
+  }
+  const int s = choose_splits(E, H, I, Tk, sms);
+  std::lock_guard<std::mutex> lock(mu);
+  const int slot = used < kSlots ? used++ : (next++ % kSlots);
+  table[slot] = Entry{E, H, I, Tk, sms, s};
+  return s;
+}
+
 int splits_for(int E, int H, int I, int Tk, int* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc != SMB_OK) return rc;
   const char* env = std::getenv("SMB_SPLIT_K");
-  int s = choose_splits(E, H, I, Tk, di.sms);
+  int s = cached_splits(E, H, I, Tk, di.sms);
   if (env != nullptr) {
     int v = std::atoi(env);
     if (v >= 1 && v <= I / 64) s = v;

@@ -25,15 +25,19 @@
 // Data movement.  Each SM's TMA engine delivers about 50 GB/s; 148 SMs together
 // saturate HBM only if TMA moves nothing but weights.  So weights come by TMA in 16 KB
 // boxes (128 rows x 64 K, 128-byte swizzle, evict-first) and the small, L2-resident token
-// tiles come by cp.async from two loader warps, written in the same swizzled layout.  The
+// tiles come by cp.async from six loader warps, written in the same swizzled layout.  The
 // gate/up token rows are first gathered into expert-major order by all CTAs in the
 // prologue (a grid counter tells the loaders when it is complete), the down rows are A2.
 //
-// Roles (256 threads, one CTA per SM):
+// Roles (384 threads, one CTA per SM):
 //   warp 0      TMA producer (one thread): weight boxes, 32 KB per stage
 //   warp 1      MMA issuer (one thread)
-//   warps 2, 3  token-tile loaders (64 threads, cp.async); warp 2 also owns TMEM
-//   warps 4..7  epilogue (128 threads = 128 TMEM lanes)
+//   warps 2..7  token-tile loaders (192 threads, cp.async); warp 2 also owns TMEM.  Six
+//               warps, because at 64 tokens per expert two loader warps moved only ~6 B
+//               per cycle (the MMA waited on token tiles 4x longer than on weights and
+//               the weight ring stayed full); measured T = 256: 536 -> 472 us per layer,
+//               ten warps no better
+//   warps 8..11 epilogue (128 threads = 128 TMEM lanes)
 // TMEM: 512 columns = two 256-column buffers (double-buffered accumulators when the
 // token tile is at most 128 wide, one buffer otherwise).
 //
@@ -48,7 +52,13 @@ namespace smb {
 
 namespace {
 
-constexpr int kThreads = 256;
+#ifndef SMB_LOADER_WARPS
+#define SMB_LOADER_WARPS 6
+#endif
+constexpr int kLoaderWarps = SMB_LOADER_WARPS;  // token-tile loader warps (2, 6 or 10)
+static_assert((2 + kLoaderWarps) % 4 == 0, "epilogue warps must start at a multiple of 4 (TMEM lane quarters)");
+constexpr int kEpiWarp0 = 2 + kLoaderWarps;      // first of the four epilogue warps
+constexpr int kThreads = 32 * (kEpiWarp0 + 4);
 constexpr int kBK = 64;                        // K elements per stage = one 128 B swizzle row
 constexpr int kBoxRows = 128;                  // rows per weight box = MMA M
 constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 16 KB
@@ -56,9 +66,9 @@ constexpr int kATileBytes = 2 * kBoxBytes;     // 256 weight rows per stage
 constexpr int kMaxN = 256;
 constexpr int kTmemCols = 512;
 constexpr int kMaxStages = 8;
-constexpr int kLoaderThreads = 64;
+constexpr int kLoaderThreads = 32 * kLoaderWarps;
 constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
-constexpr int kQueueReaders = 4;               // MMA thread, the two loader-warp leaders, epilogue leader
+constexpr int kQueueReaders = 2 + kLoaderWarps;  // MMA thread, each loader-warp leader, epilogue leader
 constexpr int kDynSmem = 227 * 1024 - 4096;  // static shared block (~3.5 KB) + this <= 227 KB
 constexpr int kPrefetchBlocks = 16;            // K blocks of the first unit warmed in L2 (512 KB)
 
@@ -429,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       s_consumed = consumed;
     }
-  } else if (warp == 2 || warp == 3) {
+  } else if (warp >= 2 && warp < kEpiWarp0) {
     // ------------------------------------------------------------ token-tile loaders
     // Lane 0 of each loader warp does every wait and broadcasts the outcome, so a wait
     // that gives up ends the whole warp together.
@@ -532,11 +542,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();
-  } else if (warp >= 4) {
+  } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;          // TMEM lane quarter this warp may read
     const int row = sub * 32 + lane;   // accumulator row = TMEM lane
-    const int et = threadIdx.x - 128;  // 0..127
+    const int et = threadIdx.x - 32 * kEpiWarp0;  // 0..127
     // A2 rows are read back by the down units and the partials by the combine moments
     // later; keep them in L2 while the weight stream (evict-first) passes through
     const uint64_t pol_keep = policy_evict_last();

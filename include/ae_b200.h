@@ -220,7 +220,7 @@ SMB_API int smb_moe_forward_gated(const void* x, const void* gate_weight, const 
  * intermediate caches with torch.empty per call.  The caller passes inputs and outputs
  * only; the workspace is a library-owned static device array of 64 MiB per GPU (held
  * until the process exits).  Sizes whose smb_moe_workspace_bytes exceed 64 MiB return
- * SMB_ERR_SCRATCH_LIMIT (Mixtral-8x7B shapes fit for every T <= 210 on a
+ * SMB_ERR_SCRATCH_LIMIT (Mixtral-8x7B shapes fit for every T <= 448 on a
  * 148-SM B200; the split-K factor, and with it the need, depends on T).  The first call
  * on each device looks up the array's device address; make it before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race. */

@@ -70,7 +70,7 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     from ae_b200 import _native
     lib = _native.load()
     E, k, H, I = 8, 2, 4096, 14336  # Mixtral-8x7B layer
-    T = 1024                         # needs ~140 MiB of workspace
+    T = 1024                         # needs ~138 MiB of workspace
     x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     logits = torch.empty(T, E, dtype=torch.bfloat16, device="cuda")
     pool = torch.empty(1, 3 * I * H, dtype=torch.bfloat16, device="cuda")
