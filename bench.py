@@ -202,7 +202,7 @@ def run_reference_arm(args, cfg, rank):
         "note": "the reference has no CPU expert path (FusedMoE.forward_cpu is unreachable); this arm runs the "
                 "oracle's CPU restatement of stack_fused_moe + select_experts",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------- GPU arm
@@ -487,7 +487,7 @@ def run_ours(args, cfg, rank, world, dev):
         "shared_expert_config": fine,
         "verify_32_layers": verify,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def bench_shared_config(cfg, dev, stream, n, hbm_peak):
@@ -718,10 +718,31 @@ def run_ep(args, cfg, rank, world, dev):
         "gpu_launches": 5 * args.steps,
         "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's real stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _stdout_to_stderr() -> None:
+    """Keep a private handle on stdout for the JSON line and send everything else that
+    writes to file descriptor 1 (library banners such as NCCL's version line, C-level
+    prints, stray Python prints) to stderr."""
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 
 
 def main():
+    _stdout_to_stderr()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -755,9 +776,6 @@ def main():
     torch.cuda.set_device(dev)
     if world > 1:
         import torch.distributed as dist
-        # NCCL's own log lines (e.g. its version banner) go to stderr: stdout carries only
-        # rank 0's JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         dist.barrier()
     try:
