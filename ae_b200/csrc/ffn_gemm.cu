@@ -70,6 +70,7 @@ constexpr int kLoaderThreads = 32 * kLoaderWarps;
 constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
 constexpr int kQueueReaders = 2 + kLoaderWarps;  // MMA thread, each loader-warp leader, epilogue leader
 constexpr int kDynSmem = 227 * 1024 - 4096;  // static shared block (~3.5 KB) + this <= 227 KB
+constexpr int kEpiStage = 4 * 2048;            // epilogue staging, 2 KB per epilogue warp, at the end
 constexpr int kPrefetchBlocks = 16;            // K blocks of the first unit warmed in L2 (512 KB)
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -93,15 +94,11 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void st_evict_last(float* p, float v, uint64_t pol) {
-  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
-}
-__device__ __forceinline__ void st_evict_last(__nv_bfloat16* p, __nv_bfloat16 v, uint64_t pol) {
-  asm volatile("st.global.L2::cache_hint.b16 [%0], %1, %2;" ::"l"(p), "h"(__bfloat16_as_ushort(v)), "l"(pol)
+// 16-byte store with an L2 eviction policy (both addresses 16-byte aligned).
+__device__ __forceinline__ void st_evict_last_v4(void* p, const uint4& v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
                : "memory");
-}
-__device__ __forceinline__ void st_evict_last(__half* p, __half v, uint64_t pol) {
-  asm volatile("st.global.L2::cache_hint.b16 [%0], %1, %2;" ::"l"(p), "h"(__half_as_ushort(v)), "l"(pol) : "memory");
 }
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -264,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stage_bytes = kATileBytes + ncap * 128;
     s_ntouched = nt;
     s_ncap = ncap;
-    s_stages = min(kMaxStages, (kDynSmem - 1024) / stage_bytes);
+    s_stages = min(kMaxStages, (kDynSmem - 1024 - kEpiStage) / stage_bytes);
   }
   tc_fence_before();
   __syncthreads();
@@ -578,34 +575,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t lane_base =
             tmem + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(buf * 256);
+        // Each warp stages its 32 rows x 16 tokens in shared memory and writes 16-byte
+        // vectors along the row (8 activations or 4 partials per store) instead of one
+        // element per thread per token.
+        uint8_t* stg = dyn_smem + (kDynSmem - kEpiStage) + sub * 2048;
         for (int c0 = 0; c0 < nlen; c0 += 16) {
           float va[16], vb[16];
           tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
           tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
+          const int nt = min(16, nlen - c0);
           if (un.phase == 1) {
-            T* out = reinterpret_cast<T*>(args.a2);
-            const int f = un.mt * 128 + row;
-            if (f < I) {
+            T* st = reinterpret_cast<T*>(stg);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 16; ++i) st[i * 32 + lane] = from_f32<T>(silu_f32(va[i]) * vb[i]);
+            __syncwarp();
+#pragma unroll
+            for (int j = lane; j < 64; j += 32) {  // 16 tokens x 4 chunks of 8 features
+              const int i = j >> 2, q = j & 3;
+              const int p = row0 + n0 + c0 + i;
+              const int f = un.mt * 128 + sub * 32 + q * 8;
+              if (i < nt && p >= 0 && p < args.Tk && f < I) {
+                st_evict_last_v4(reinterpret_cast<T*>(args.a2) + static_cast<size_t>(p) * I + f,
+                                 *reinterpret_cast<const uint4*>(st + i * 32 + q * 8), pol_keep);
+              }
+            }
+            __syncwarp();
+          } else {
+            float* st = reinterpret_cast<float*>(stg);
+            auto put_rows = [&](const float (&v)[16], int half) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) st[i * 32 + lane] = v[i];
+              __syncwarp();
+#pragma unroll
+              for (int j = lane; j < 128; j += 32) {  // 16 tokens x 8 chunks of 4 rows
+                const int i = j >> 3, q = j & 7;
                 const int p = row0 + n0 + c0 + i;
-                if (c0 + i < nlen && p >= 0 && p < args.Tk) {
-                  st_evict_last(out + static_cast<size_t>(p) * I + f, from_f32<T>(silu_f32(va[i]) * vb[i]), pol_keep);
+                const int h = un.mt * 256 + half * 128 + sub * 32 + q * 4;
+                if (i < nt && p >= 0 && p < args.Tk && h < H) {
+                  st_evict_last_v4(args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H + h,
+                                   *reinterpret_cast<const uint4*>(st + i * 32 + q * 4), pol_keep);
                 }
               }
-            }
-          } else {
-            const int h0 = un.mt * 256 + row;
-            const int h1 = h0 + 128;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int p = row0 + n0 + c0 + i;
-              if (c0 + i < nlen && p >= 0 && p < args.Tk) {
-                float* dst = args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H;
-                if (h0 < H) st_evict_last(dst + h0, va[i], pol_keep);
-                if (h1 < H) st_evict_last(dst + h1, vb[i], pol_keep);
-              }
-            }
+              __syncwarp();
+            };
+            put_rows(va, 0);
+            put_rows(vb, 1);
           }
         }
         tc_fence_before();
