@@ -38,6 +38,14 @@ SIGNATURES = {
     "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_noalloc": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "smb_ep_arena_bytes": (_S, [_I, _I, _I, _I]),
+    "smb_ep_ipc_alloc": (_I, [_S, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "smb_ep_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "smb_ep_ipc_close": (_I, [_P]),
+    "smb_ep_ipc_free": (_I, [_P]),
+    "smb_moe_ep_dispatch_p2p": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
+    "smb_moe_ep_experts_p2p": (_I, [_I, _I, _I, _P, _P, _L, _P, _I, _I, _I, _I, _P, _S, _P]),
+    "smb_moe_ep_combine_p2p": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_shared": (_I, [_P, _P, _I, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P,
                                     _S, _P]),
     "smb_moe_workspace_init": (_I, [_P, _S, _P]),

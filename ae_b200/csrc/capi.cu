@@ -229,10 +229,37 @@ int gate_grid(int T, int sms) {
 }
 
 struct EpLayout {
-  void* send = nullptr;        // dispatch: write rows into [G][C+1][H]
+  void* send = nullptr;        // dispatch mode marker (rows go to link.chunk[d])
   const void* recv = nullptr;  // experts: tokens are the payload rows of [G][C+1][H]
   int G = 0, C = 0, Eloc = 1;
+  EpLink link{};
 };
+
+// Pointers of the peer-memory transport for rank `rank` of G, from the arenas of all
+// ranks (arenas[rank] is this rank's own).
+struct EpPeers {
+  uint8_t* arena[kMaxRanks];
+  EpArena A;
+  int G, rank;
+  size_t row_bytes;
+};
+
+int ep_peers(void* const* arenas, int G, int rank, int C, int H, int dtype, EpPeers* P) {
+  if (G < 1 || G > kMaxRanks || rank < 0 || rank >= G || C < 1) return SMB_ERR_SHAPE;
+  if (arenas == nullptr) return SMB_ERR_NULL;
+  P->A = make_ep_arena(G, C, H, elem_bytes_of(dtype));
+  P->G = G;
+  P->rank = rank;
+  P->row_bytes = static_cast<size_t>(H) * elem_bytes_of(dtype);
+  for (int r = 0; r < G; ++r) {
+    if (arenas[r] == nullptr) return SMB_ERR_NULL;
+    if (!aligned(arenas[r], kAlign)) return SMB_ERR_ALIGN;
+    P->arena[r] = static_cast<uint8_t*>(arenas[r]);
+  }
+  return SMB_OK;
+}
+int* ep_ctrl(const EpPeers& P, int r) { return reinterpret_cast<int*>(P.arena[r] + P.A.ctrl); }
+int* ep_flags(const EpPeers& P, int r) { return reinterpret_cast<int*>(P.arena[r] + P.A.flags); }
 
 // Router gate inputs of the gated launch (x is the token matrix passed to do_route).
 struct GateIn {
@@ -257,9 +284,10 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   if (logits != nullptr && logits_dtype != SMB_DTYPE_F16 && logits_dtype != SMB_DTYPE_BF16 &&
       logits_dtype != SMB_DTYPE_F32)
     return SMB_ERR_DTYPE;
-  if (T == 0) return SMB_OK;
-  if (x == nullptr) return SMB_ERR_NULL;
-  if (gate == nullptr && logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr))
+  // over peer memory a rank without tokens still sends its (empty) chunks and flags
+  if (T == 0 && !ep.link.p2p) return SMB_OK;
+  if (x == nullptr && T > 0) return SMB_ERR_NULL;
+  if (T > 0 && gate == nullptr && logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr))
     return SMB_ERR_NULL;
   if (gate != nullptr && (gate->weight == nullptr || ep.send != nullptr || ep.recv != nullptr)) return SMB_ERR_NULL;
   if (!aligned(x, 16)) return SMB_ERR_ALIGN;
@@ -297,6 +325,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.ep_G = ep.G;
   a.ep_C = ep.C;
   a.ep_Eloc = ep.Eloc;
+  a.link = ep.link;
   const int Tk = T * k;
   if (gate != nullptr) {
     // gate + routing in one launch: the gate's CTAs each take ceil(T / SMs) tokens, the
@@ -379,13 +408,13 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
 }
 
 int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
-               cudaStream_t stream) {
+               cudaStream_t stream, int ep_C = 0, const EpLink* link = nullptr) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
   if (T == 0) return SMB_OK;
-  if (out == nullptr) return SMB_ERR_NULL;
-  if (!aligned(out, 16)) return SMB_ERR_ALIGN;
+  if (ep_C == 0 && out == nullptr) return SMB_ERR_NULL;  // the expert side writes through link->chunk
+  if (out != nullptr && !aligned(out, 16)) return SMB_ERR_ALIGN;
   CombineArgs a{};
   a.part = at<const float>(ws, L.part);
   a.inv = at<const int32_t>(ws, L.inv);
@@ -395,6 +424,8 @@ int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const vo
   a.k = k;
   a.H = H;
   a.splits = L.splits;
+  a.ep_C = ep_C;
+  if (link != nullptr) a.link = *link;
   cudaError_t err = launch_combine(a, dtype == SMB_DTYPE_BF16, stream, pdl_enabled());
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
@@ -498,11 +529,16 @@ int smb_moe_ep_dispatch(const void* router_logits, int logits_dtype, const void*
   if (G < 1 || E % G != 0 || C < T * k || (E / G) * 4 > H * 2) return SMB_ERR_SHAPE;
   if (send == nullptr || (router_logits == nullptr && T > 0)) return SMB_ERR_NULL;
   if (!aligned(send, 16)) return SMB_ERR_ALIGN;
+  if (G > kMaxRanks) return SMB_ERR_SHAPE;
   EpLayout ep;
   ep.send = send;
   ep.G = G;
   ep.C = C;
   ep.Eloc = E / G;
+  ep.link.nranks = G;
+  for (int d = 0; d < G; ++d) {
+    ep.link.chunk[d] = static_cast<uint8_t*>(send) + static_cast<size_t>(d) * (C + 1) * H * elem_bytes_of(dtype);
+  }
   return do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize, topk_weights,
                   topk_ids, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream), ep);
 }
@@ -525,7 +561,140 @@ int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t
   if (rc != SMB_OK) return rc;
   rc = do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
-  return do_combine(out_rows, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s);
+  if (G > kMaxRanks) return SMB_ERR_SHAPE;
+  EpLink link{};
+  link.nranks = G;
+  for (int src = 0; src < G; ++src) {
+    link.chunk[src] = static_cast<uint8_t*>(out_rows) + static_cast<size_t>(src) * C * H * elem_bytes_of(dtype);
+  }
+  return do_combine(out_rows, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, C, &link);
+}
+
+size_t smb_ep_arena_bytes(int G, int C, int H, int dtype) {
+  if (G < 1 || G > kMaxRanks || C < 1 || H < 128 || elem_bytes_of(dtype) == 0) return 0;
+  return make_ep_arena(G, C, H, elem_bytes_of(dtype)).total;
+}
+
+int smb_ep_ipc_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (dev_ptr == nullptr || ipc_handle == nullptr) return SMB_ERR_NULL;
+  if (bytes == 0) return SMB_ERR_SHAPE;
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, bytes);
+  if (err != cudaSuccess) return cuda_fail(err);
+  err = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(&h, p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(err);
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return SMB_OK;
+}
+
+int smb_ep_ipc_open(const void* ipc_handle, void** peer_ptr) {
+  if (ipc_handle == nullptr || peer_ptr == nullptr) return SMB_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t err = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_ep_ipc_close(void* peer_ptr) {
+  if (peer_ptr == nullptr) return SMB_ERR_NULL;
+  cudaError_t err = cudaIpcCloseMemHandle(peer_ptr);
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_ep_ipc_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return SMB_ERR_NULL;
+  cudaError_t err = cudaFree(dev_ptr);
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_moe_ep_dispatch_p2p(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E,
+                            int k, int H, int I, int renormalize, int G, int rank, int C, void* const* arenas,
+                            float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (G < 1 || E % G != 0 || C < T * k || (E / G) * 4 > H * 2) return SMB_ERR_SHAPE;
+  if (router_logits == nullptr && T > 0) return SMB_ERR_NULL;
+  EpPeers P;
+  int rc = ep_peers(arenas, G, rank, C, H, dtype, &P);
+  if (rc != SMB_OK) return rc;
+  EpLayout ep;
+  ep.send = P.arena[rank];  // dispatch mode; the rows go to the destinations' receive chunks
+  ep.G = G;
+  ep.C = C;
+  ep.Eloc = E / G;
+  ep.link.nranks = G;
+  ep.link.p2p = 1;
+  ep.link.ctrl = ep_ctrl(P, rank);
+  for (int d = 0; d < G; ++d) {
+    ep.link.chunk[d] = P.arena[d] + P.A.recv + static_cast<size_t>(rank) * (C + 1) * P.row_bytes;
+    ep.link.flag[d] = ep_flags(P, d) + rank;
+  }
+  return do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize, topk_weights,
+                  topk_ids, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream), ep);
+}
+
+int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const void* pool, int64_t num_pages,
+                           const int64_t* page_of_expert, int dtype, int E_loc, int H, int I, void* ws,
+                           size_t ws_bytes, smb_stream_t stream) {
+  if (E_loc < 1 || E_loc * 4 > H * 2) return SMB_ERR_SHAPE;
+  EpPeers P;
+  int rc = ep_peers(arenas, G, rank, C, H, dtype, &P);
+  if (rc != SMB_OK) return rc;
+  const int T = G * C;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const void* recv = P.arena[rank] + P.A.recv;
+  EpLayout ep;
+  ep.recv = recv;
+  ep.G = G;
+  ep.C = C;
+  ep.Eloc = E_loc;
+  ep.link.nranks = G;
+  ep.link.p2p = 1;
+  ep.link.ctrl = ep_ctrl(P, rank);
+  ep.link.wait_flags = ep_flags(P, rank);  // one flag per source
+  rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
+                ws_bytes, s, ep);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
+  if (rc != SMB_OK) return rc;
+  EpLink link{};
+  link.nranks = G;
+  link.p2p = 1;
+  link.ctrl = ep_ctrl(P, rank);
+  for (int src = 0; src < G; ++src) {
+    link.chunk[src] = P.arena[src] + P.A.back + static_cast<size_t>(rank) * C * P.row_bytes;
+    link.flag[src] = ep_flags(P, src) + kEpReturnFlags + rank;
+  }
+  return do_combine(nullptr, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, C, &link);
+}
+
+int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int I, int G, int rank, int C,
+                           void* const* arenas, const void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (G < 1 || E % G != 0 || C < T * k) return SMB_ERR_SHAPE;
+  EpPeers P;
+  int rc = ep_peers(arenas, G, rank, C, H, dtype, &P);
+  if (rc != SMB_OK) return rc;
+  WsLayout L;
+  rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  if (rc != SMB_OK) return rc;
+  if (out == nullptr && T > 0) return SMB_ERR_NULL;
+  if (T > 0 && !aligned(out, 16)) return SMB_ERR_ALIGN;
+  EpLink link{};
+  link.nranks = G;
+  link.p2p = 1;
+  link.ctrl = ep_ctrl(P, rank);
+  link.wait_flags = ep_flags(P, rank) + kEpReturnFlags;  // one flag per expert rank
+  // T = 0 still takes part: it waits for the returns and advances this rank's epoch
+  cudaError_t err = launch_combine_rows(P.arena[rank] + P.A.back, at<const int32_t>(ws, L.inv),
+                                        at<const float>(ws, L.w), out, T, k, H, dtype == SMB_DTYPE_BF16,
+                                        reinterpret_cast<cudaStream_t>(stream), pdl_enabled(),
+                                        at<const int32_t>(ws, L.ids), at<const int32_t>(ws, L.expert_off), C, E / G,
+                                        &link, at<int>(ws, L.status));
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
 int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int k, int H, int I, int G, int C,

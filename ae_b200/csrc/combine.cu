@@ -19,13 +19,9 @@ namespace {
 constexpr int kCombineThreads = 256;
 
 template <typename TO>
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
-  pdl_wait_prior_grids();
-  pdl_launch_dependents();
-  const int t = blockIdx.y;
-  const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
-  if (h4 * 4 >= a.H) return;
+__device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4) {
   const size_t Tk = static_cast<size_t>(a.T) * a.k;
+  if (a.ep_C > 0 && a.inv[t] < 0) return;  // expert side of the exchange: an empty payload slot
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < a.k; ++j) {
     const size_t f = static_cast<size_t>(t) * a.k + j;
@@ -61,7 +57,15 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     acc.z += wj * s.z;
     acc.w += wj * s.w;
   }
-  TO* out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H + static_cast<size_t>(h4) * 4;
+  TO* out;
+  if (a.ep_C > 0) {
+    // row t = s*C + i of the exchange goes back to source s (local buffer for NCCL, the
+    // source's return buffer over peer memory)
+    const int s = t / a.ep_C;
+    out = reinterpret_cast<TO*>(a.link.chunk[s]) + static_cast<size_t>(t - s * a.ep_C) * a.H;
+  } else {
+    out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H;
+  }
   union {
     TO h[4];
     uint2 u;
@@ -70,23 +74,31 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   pack.h[1] = from_f32<TO>(acc.y);
   pack.h[2] = from_f32<TO>(acc.z);
   pack.h[3] = from_f32<TO>(acc.w);
-  *reinterpret_cast<uint2*>(out) = pack.u;
+  *reinterpret_cast<uint2*>(out + static_cast<size_t>(h4) * 4) = pack.u;
 }
 
-// Weighted combine of per-slot rows: out[t, h] = sum_j w[t, j] * rows[inv[t*k+j]][h], in
-// that order in fp32, rows in the storage dtype (the expert outputs of the expert-parallel
-// path returned by the all-to-all, in dispatch order).
 template <typename TO>
-__global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const void* rows_v, const int32_t* inv,
-                                                                        const float* w, void* out_v, int T, int k,
-                                                                        int H, const int32_t* ids,
-                                                                        const int32_t* expert_off, int ep_C,
-                                                                        int ep_Eloc) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
   pdl_wait_prior_grids();
   pdl_launch_dependents();
   const int t = blockIdx.y;
   const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
-  if (h4 * 4 >= H) return;
+  if (h4 * 4 < a.H) combine_one<TO>(a, t, h4);
+  // over peer memory: when every row has been sent, raise this rank's return flag at
+  // each source
+  if (a.link.p2p) {
+    __shared__ int s_last;
+    if (last_cta_of_grid(a.link.ctrl + 2, &s_last)) {
+      const int epoch = a.link.ctrl[0] + 1;
+      for (int s = threadIdx.x; s < a.link.nranks; s += kCombineThreads) st_release_sys(a.link.flag[s], epoch);
+    }
+  }
+}
+
+template <typename TO>
+__device__ __forceinline__ void combine_rows_one(const void* rows_v, const int32_t* inv, const float* w, void* out_v,
+                                                 int T, int k, int H, const int32_t* ids, const int32_t* expert_off,
+                                                 int ep_C, int ep_Eloc, int t, int h4) {
   const size_t Tk = static_cast<size_t>(T) * k;
   const TO* rows = reinterpret_cast<const TO*>(rows_v);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -105,7 +117,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
       uint2 u;
       TO h[4];
     } v;
-    v.u = __ldg(reinterpret_cast<const uint2*>(rows + row * H) + h4);
+    // L2 loads: over peer memory the rows were written by other GPUs while this grid ran
+    v.u = __ldcg(reinterpret_cast<const uint2*>(rows + row * H) + h4);
     acc.x += wj * to_f32<TO>(v.h[0]);
     acc.y += wj * to_f32<TO>(v.h[1]);
     acc.z += wj * to_f32<TO>(v.h[2]);
@@ -121,6 +134,35 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
   pack.h[3] = from_f32<TO>(acc.w);
   *reinterpret_cast<uint2*>(reinterpret_cast<TO*>(out_v) + static_cast<size_t>(t) * H + static_cast<size_t>(h4) * 4) =
       pack.u;
+}
+
+// Weighted combine of per-slot rows: out[t, h] = sum_j w[t, j] * rows[inv[t*k+j]][h], in
+// that order in fp32, rows in the storage dtype (the expert outputs of the expert-parallel
+// path returned by the all-to-all, in dispatch order).
+template <typename TO>
+__global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const void* rows_v, const int32_t* inv,
+                                                                        const float* w, void* out_v, int T, int k,
+                                                                        int H, const int32_t* ids,
+                                                                        const int32_t* expert_off, int ep_C,
+                                                                        int ep_Eloc, const EpLink link, int* status) {
+  pdl_wait_prior_grids();
+  pdl_launch_dependents();
+  const int t = blockIdx.y;
+  const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
+  __shared__ int s_ok, s_last;
+  if (link.p2p) {
+    // the returned rows are complete once every expert rank raised its flag to this epoch
+    if (threadIdx.x == 0) {
+      s_ok = wait_flags_sys(link.wait_flags, link.nranks, link.ctrl[0] + 1) ? 1 : 0;
+      if (!s_ok && blockIdx.x == 0 && blockIdx.y == 0) record_status(status, kDevTimeout);
+    }
+    __syncthreads();
+  }
+  if (h4 * 4 < H && t < T) combine_rows_one<TO>(rows_v, inv, w, out_v, T, k, H, ids, expert_off, ep_C, ep_Eloc, t, h4);
+  if (link.p2p) {
+    // every CTA has read its rows: this call is finished on this rank, advance the epoch
+    if (last_cta_of_grid(link.ctrl + 3, &s_last) && threadIdx.x == 0) link.ctrl[0] = link.ctrl[0] + 1;
+  }
 }
 
 constexpr int kAlignThreads = 1024;
@@ -197,11 +239,14 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
                                 int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids,
-                                const int32_t* expert_off, int ep_C, int ep_Eloc) {
+                                const int32_t* expert_off, int ep_C, int ep_Eloc, const EpLink* link,
+                                int* status) {
+  EpLink lk{};
+  if (link != nullptr) lk = *link;
   const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_rows_kernel<__nv_bfloat16>)
                         : reinterpret_cast<const void*>(&combine_rows_kernel<__half>);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((H / 4 + kCombineThreads - 1) / kCombineThreads, T);
+  cfg.gridDim = dim3((H / 4 + kCombineThreads - 1) / kCombineThreads, T > 0 ? T : 1);  // T = 0: flags only
   cfg.blockDim = dim3(kCombineThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -210,7 +255,8 @@ cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<void**>(&rows), const_cast<int32_t**>(&inv), const_cast<float**>(&w), &out, &T,
-                    &k, &H, const_cast<int32_t**>(&ids), const_cast<int32_t**>(&expert_off), &ep_C, &ep_Eloc};
+                    &k, &H, const_cast<int32_t**>(&ids), const_cast<int32_t**>(&expert_off), &ep_C, &ep_Eloc,
+                    &lk, &status};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

@@ -28,6 +28,48 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// System-scope flag access for the peer-memory exchange (flags live in another GPU's
+// memory or are written from one).
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait, bounded, until flags[0..n) are all >= epoch (called by one thread).
+__device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, int epoch) {
+  const uint64_t t0 = global_timer_ns();
+  for (int s = 0; s < n; ++s) {
+    while (ld_acquire_sys(flags + s) < epoch) {
+      if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
+      __nanosleep(100);
+    }
+  }
+  return true;
+}
+
+// Called by every thread of every CTA once its global / peer stores are issued: true in
+// the CTA that finished last (its stores and all others' are then visible system-wide);
+// that CTA leaves the ticket at 0 for the next launch.  No CTA waits for another.
+__device__ __forceinline__ bool last_cta_of_grid(int* ticket, int* s_flag) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int n = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+    *s_flag = atomicAdd(ticket, 1) == n - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  const bool last = *s_flag != 0;
+  if (last) {
+    __threadfence_system();
+    if (threadIdx.x == 0) *ticket = 0;
+  }
+  return last;
+}
+
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }

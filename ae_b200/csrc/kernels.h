@@ -49,6 +49,21 @@ struct FfnArgs {
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
                             const CUtensorMap& w2, const FfnArgs& args);
 
+// Expert-parallel exchange over peer memory.  Rank r's arena (same layout on every rank,
+// mapped by its peers through CUDA IPC) holds a control block (epoch, CTA tickets), the
+// flags its peers set, and the receive / return chunks.  chunk[d] is where this kernel
+// puts the rows meant for rank d; with the NCCL transport it points into the local send
+// buffer instead, and no flag is set or waited for.
+constexpr int kMaxRanks = 8;
+struct EpLink {
+  void* chunk[kMaxRanks];  // per destination: base of this rank's chunk in its buffer
+  int* flag[kMaxRanks];    // per destination: the flag slot this rank sets there (p2p)
+  int* ctrl;               // local control block: [0] epoch of the last finished call, [1..3] tickets
+  const int* wait_flags;   // local flags to wait for (one per peer), p2p receive sides
+  int nranks;
+  int p2p;                 // 1: peer memory with flags, 0: NCCL moves the buffers
+};
+
 struct RouteArgs {
   const void* logits;      // [T, E] or nullptr (routing given)
   int logits_dtype;        // SMB_DTYPE_*
@@ -72,9 +87,10 @@ struct RouteArgs {
   int rows_per_cta;
   // expert-parallel exchange layout: G chunks of (1 header row + C payload rows) x H; a
   // header row holds the chunk's per-local-expert counts as int32 in its first bytes
-  void* ep_send;           // dispatch: gather rows here (dst-major, capacity C)
+  void* ep_send;           // dispatch: gather rows into link.chunk[d] (non-null marks dispatch mode)
   const void* ep_recv;     // receive: tokens are the payload rows, ids come from the headers
   int ep_G, ep_C, ep_Eloc;
+  EpLink link;
 };
 
 // Router gate fused with the routing (gate_route_kernel): logits = x W^T of
@@ -103,6 +119,10 @@ struct CombineArgs {
   const float* w;       // [Tk]
   void* out;            // [T, H] storage dtype
   int T, k, H, splits;
+  // expert side of the exchange (ep_C > 0): row t = s*C + i goes to link.chunk[s] + i rows;
+  // rows without a slot are skipped
+  int ep_C;
+  EpLink link;
 };
 
 cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream, bool pdl);
@@ -111,7 +131,8 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 // slot f reads row (ids[f] / ep_Eloc) * ep_C + inv[f] - expert_off[(ids[f] / ep_Eloc) * ep_Eloc]
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
                                 int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids = nullptr,
-                                const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1);
+                                const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1,
+                                const EpLink* link = nullptr, int* status = nullptr);
 
 cudaError_t launch_align(const int32_t* ids, int numel, int E, int block, int32_t* sorted_ids, int32_t* expert_ids,
                          int32_t* num_post_pad, int max_blocks, cudaStream_t stream);

@@ -67,6 +67,30 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   return L;
 }
 
+// Exchange arena of the peer-memory expert-parallel transport (one per rank, the same
+// layout on every rank; peers write into it through CUDA IPC mappings):
+//   ctrl  int32 [64]      [0] epoch = number of finished layer calls, [1..3] CTA tickets of
+//                         the dispatch, expert-combine and final-combine kernels
+//   flags int32 [2 x 8]   [s] source s finished writing its chunk of this rank's recv for
+//                         epoch e (value e); [8 + d] expert rank d finished writing its
+//                         chunk of this rank's back
+//   recv  [G][C+1][H]     chunk s = header row (counts per local expert) + C payload rows
+//                         from source s
+//   back  [G][C][H]       chunk d = expert outputs returned by expert rank d
+struct EpArena {
+  size_t ctrl, flags, recv, back, total;
+};
+inline EpArena make_ep_arena(int G, int C, int H, int elem_bytes) {
+  EpArena A{};
+  A.ctrl = 0;
+  A.flags = 256;
+  A.recv = 1024;
+  A.back = A.recv + align_up(static_cast<size_t>(G) * (C + 1) * H * elem_bytes, kAlign);
+  A.total = A.back + align_up(static_cast<size_t>(G) * C * H * elem_bytes, kAlign);
+  return A;
+}
+constexpr int kEpReturnFlags = 8;  // offset of the return flags in the flag block
+
 // Split-K factor of the down projection, chosen by simulating the FFN kernel's dynamic
 // unit queue on `num_sms` SMs.  More splits make smaller down units (256 rows x I/S), so
 // the run ends with less idle time, but add fp32 partials (S x Tk x H x 4 B) that the
@@ -80,11 +104,11 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
 inline int choose_splits(int E, int H, int I, int Tk, int num_sms) {
   const double rate = 44e9, hbm = 6.5e12, part_factor = 2.0;
   const int kb2 = I / 64;
+  const int et = E < Tk ? E : (Tk > 0 ? Tk : 1);
+  const int sms = num_sms > 0 ? num_sms : 1;
   const int m1 = (I + 127) / 128;
   const int m2 = (H + 255) / 256;
-  const int et = E < Tk ? E : (Tk > 0 ? Tk : 1);
   const int smax = kb2 < 16 ? kb2 : 16;
-  const int sms = num_sms > 0 ? num_sms : 1;
   typedef std::priority_queue<double, std::vector<double>, std::greater<double>> Heap;
   // phase 1 is the same for every S: simulate it once
   Heap base;

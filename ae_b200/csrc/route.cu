@@ -12,7 +12,9 @@
 // (per-warp histograms, a scan, then match_any ranks inside 32-slot chunks).  The FFN
 // kernel reads token rows through the permutation, so nothing is copied here, except
 // for the expert-parallel dispatch: then every CTA recomputes the (cheap) routing and
-// copies its share of the token rows into the send buffer of the exchange.
+// copies its share of the token rows into the destination chunks of the exchange (a
+// local send buffer for NCCL, or the destinations' receive buffers over peer memory,
+// followed by a flag per destination).
 #include <cfloat>
 #include <climits>
 
@@ -157,6 +159,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   int32_t* s_cnt = reinterpret_cast<int32_t*>(s_w + Tk); // [warps][E]
   int32_t* s_off = s_cnt + kRouteWarps * E;              // [E+1]
   __shared__ int s_bad;
+  __shared__ int s_ready;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -188,16 +191,31 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     }
   } else if (a.ep_recv != nullptr) {
     // expert side of the exchange: payload row f = s*C + i of source s belongs to the
-    // local expert whose run of the source's header counts holds i (k = 1, weight 1)
+    // local expert whose run of the source's header counts holds i (k = 1, weight 1).
+    // Over peer memory the chunks are complete once every source has raised its flag to
+    // this call's epoch; if one does not within the wait budget, no row is taken.
     const size_t row_bytes = static_cast<size_t>(a.H) * 2;
+    if (tid == 0) {
+      s_ready = 1;
+      if (a.link.p2p) {
+        s_ready = wait_flags_sys(a.link.wait_flags, a.link.nranks, a.link.ctrl[0] + 1) ? 1 : 0;
+        if (!s_ready) record_status(a.status, kDevTimeout);
+      }
+    }
+    __syncthreads();
     for (int f = tid; f < Tk; f += kRouteThreads) {
+      if (!s_ready) {
+        s_ids[f] = -1;
+        s_w[f] = 0.0f;
+        continue;
+      }
       const int src = f / a.ep_C;
       const int i = f - src * a.ep_C;
       const int32_t* hdr = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(a.ep_recv) +
                                                             static_cast<size_t>(src) * (a.ep_C + 1) * row_bytes);
       int id = -1, acc = 0;
       for (int e = 0; e < a.ep_Eloc; ++e) {
-        const int c = hdr[e];
+        const int c = __ldcg(hdr + e);  // written by the source GPU while this grid waited
         if (i < acc + c) {
           id = e;
           break;
@@ -302,11 +320,9 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     for (int e = tid; e <= E; e += kRouteThreads) a.expert_off[e] = s_off[e];
     if (a.ep_send != nullptr) {
       // header row of each destination chunk: counts of that destination's experts
-      const size_t row_bytes = static_cast<size_t>(a.H) * 2;
       for (int e = tid; e < E; e += kRouteThreads) {
         const int d = e / a.ep_Eloc;
-        int32_t* hdr = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(a.ep_send) +
-                                                  static_cast<size_t>(d) * (a.ep_C + 1) * row_bytes);
+        int32_t* hdr = reinterpret_cast<int32_t*>(a.link.chunk[d]);
         hdr[e - d * a.ep_Eloc] = s_off[e + 1] - s_off[e];
       }
     }
@@ -332,18 +348,19 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   // layout, all threads on all rows, four independent 16-byte loads in flight per thread
   if (a.ep_send == nullptr) return;  // the FFN reads token rows through the permutation
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.ep_recv != nullptr ? a.ep_recv : a.x);
-  uint4* xdst = reinterpret_cast<uint4*>(a.ep_send);
+  const size_t row_bytes_out = static_cast<size_t>(vec_per_row) * 16;
   // source row of token t: plain, or payload row t of the exchange layout
   auto src_row = [&](int t) -> size_t {
     if (a.ep_recv == nullptr) return static_cast<size_t>(t);
     const int s = t / a.ep_C;
     return static_cast<size_t>(s) * (a.ep_C + 1) + 1 + (t - s * a.ep_C);
   };
-  // destination row of flat slot f at expert-major position p
-  auto dst_row = [&](int f, int p) -> size_t {
-    if (a.ep_send == nullptr) return static_cast<size_t>(p);
+  // destination row of flat slot f at expert-major position p: payload row
+  // p - (first position of the destination's experts) of the destination's chunk
+  auto dst_row = [&](int f, int p) -> uint4* {
     const int d = s_ids[f] / a.ep_Eloc;
-    return static_cast<size_t>(d) * (a.ep_C + 1) + 1 + (p - s_off[d * a.ep_Eloc]);
+    return reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.link.chunk[d]) +
+                                    static_cast<size_t>(1 + p - s_off[d * a.ep_Eloc]) * row_bytes_out);
   };
   const int nvec = (g1 - g0) * vec_per_row;
   for (int base = tid; base < nvec; base += 4 * kRouteThreads) {
@@ -361,8 +378,17 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        if (s_pos[f] >= 0) xdst[dst_row(f, s_pos[f]) * vec_per_row + (i % vec_per_row)] = v[j];
+        if (s_pos[f] >= 0) dst_row(f, s_pos[f])[i % vec_per_row] = v[j];
       }
+    }
+  }
+  // over peer memory: once every CTA's rows (and CTA 0's headers) have landed, tell each
+  // destination that this rank's chunk for the current call is complete
+  if (a.link.p2p) {
+    __shared__ int s_last;
+    if (last_cta_of_grid(a.link.ctrl + 1, &s_last)) {
+      const int epoch = a.link.ctrl[0] + 1;
+      for (int d = tid; d < a.link.nranks; d += kRouteThreads) st_release_sys(a.link.flag[d], epoch);
     }
   }
 }

@@ -20,8 +20,17 @@ used (``specmoe/utils/server_args.py:148,202``).  Here rank r owns experts
 One process per GPU; the compute steps go through a backend object, so the exchange logic
 runs the same with the CUDA library (``CudaBackend``) or with any other implementation of
 the three steps.
+
+``transport="p2p"`` moves the rows without a collective library: every rank owns an
+exchange arena that its peers map through CUDA IPC (``PeerTransport``); the dispatch
+kernel writes each destination's rows straight into that destination's arena over NVLink
+and raises a flag there, the expert kernels wait for the flags, run the local experts and
+write every row's output back into its source's arena (another flag), and the combine
+waits for those.  Three library calls per layer call, no NCCL launch, graph-capturable.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -89,6 +98,85 @@ class CudaBackend:
         return out
 
 
+class PeerTransport:
+    """This rank's exchange arena plus its peers' arenas mapped through CUDA IPC
+    (``smb_ep_ipc_*`` in ``include/ae_b200.h``).  Collective: every rank of ``group``
+    constructs it with the same (C, H, dtype)."""
+
+    def __init__(self, C: int, H: int, dtype: torch.dtype, device, group=None):
+        from . import _native, ops
+        self.group = group
+        self.G = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        lib = _native.load()
+        nbytes = int(lib.smb_ep_arena_bytes(self.G, C, H, ops.storage_code(dtype)))
+        if nbytes == 0:
+            raise ValueError(f"no exchange arena for G={self.G} C={C} H={H} (at most 8 ranks)")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(device):
+            _native.check("smb_ep_ipc_alloc", lib.smb_ep_ipc_alloc(nbytes, ctypes.byref(own), handle))
+        self.own = own.value
+        handles = [None] * self.G
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.arenas = (ctypes.c_void_p * self.G)()
+        self.opened = []
+        with torch.cuda.device(device):
+            for r in range(self.G):
+                if r == self.rank:
+                    self.arenas[r] = self.own
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                peer = ctypes.c_void_p()
+                _native.check("smb_ep_ipc_open", lib.smb_ep_ipc_open(h, ctypes.byref(peer)))
+                self.arenas[r] = peer.value
+                self.opened.append(peer.value)
+        self.arenas_ptr = ctypes.cast(self.arenas, ctypes.c_void_p)
+        dist.barrier(group)
+
+    def close(self):
+        """Unmap the peers' arenas and free this rank's (collective)."""
+        from . import _native
+        lib = _native.load()
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        for p in self.opened:
+            lib.smb_ep_ipc_close(ctypes.c_void_p(p))
+        self.opened = []
+        dist.barrier(self.group)
+        if self.own:
+            lib.smb_ep_ipc_free(ctypes.c_void_p(self.own))
+            self.own = None
+
+
+class P2PBackend(CudaBackend):
+    """The three steps over peer memory (``smb_moe_ep_*_p2p``): the exchange happens inside
+    the kernels, so ``ExpertParallelMoE`` makes no collective call."""
+
+    def __init__(self, E, k, H, I, dtype, device, transport: PeerTransport, renormalize: bool = True):
+        super().__init__(E, k, H, I, dtype, device, renormalize)
+        self.t = transport
+
+    def layer(self, x, logits, G, C, pool, pages, num_local):
+        from . import _native, ops
+        T = x.shape[0]
+        nb = ops.workspace_bytes(max(T, 1), self.E, self.k, self.H, self.I, self.dtype)
+        ws = self._buf(("ws_src", T), nbytes=nb)
+        nbe = ops.workspace_bytes(G * C, num_local, 1, self.H, self.I, self.dtype)
+        wse = self._buf(("ws_exp", G, C), nbytes=nbe)
+        out = self._buf(("out", T), shape=(T, self.H), dtype=self.dtype)
+        st = self._stream()
+        a = self.t.arenas_ptr
+        _native.call("smb_moe_ep_dispatch_p2p", logits.data_ptr() if T else None, ops.logits_code(logits.dtype),
+                     x.data_ptr() if T else None, self.code, T, self.E, self.k, self.H, self.I,
+                     int(self.renormalize), G, self.t.rank, C, a, None, None, ws.data_ptr(), ws.numel(), st)
+        _native.call("smb_moe_ep_experts_p2p", G, self.t.rank, C, a, pool.data_ptr(), pool.shape[0],
+                     pages.data_ptr(), self.code, num_local, self.H, self.I, wse.data_ptr(), wse.numel(), st)
+        _native.call("smb_moe_ep_combine_p2p", out.data_ptr() if T else None, self.code, T, self.E, self.k,
+                     self.H, self.I, G, self.t.rank, C, a, ws.data_ptr(), ws.numel(), st)
+        return out
+
+
 class ExpertParallelMoE:
     """MoE layer over G ranks, E/G experts each (``pool`` holds this rank's pages).
 
@@ -99,7 +187,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
-                 pool: torch.Tensor, max_tokens: int, group=None, backend=None, renormalize: bool = True):
+                 pool: torch.Tensor, max_tokens: int, group=None, backend=None, renormalize: bool = True,
+                 transport: str = "nccl"):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -115,6 +204,15 @@ class ExpertParallelMoE:
         self.pages = torch.arange(self.E_loc, dtype=torch.int64, device=pool.device)
         self.max_tokens = int(max_tokens)
         self.C = self.max_tokens * top_k  # rows reserved per (source, destination) pair
+        self.transport = None
+        if transport == "p2p":
+            if backend is not None:
+                raise ValueError("transport='p2p' runs the library's own kernels; no backend can be given")
+            self.transport = PeerTransport(self.C, hidden_size, pool.dtype, pool.device, group)
+            backend = P2PBackend(num_experts, top_k, hidden_size, intermediate_size, pool.dtype, pool.device,
+                                 self.transport, renormalize)
+        elif transport != "nccl":
+            raise ValueError(f"transport must be 'nccl' or 'p2p', not {transport!r}")
         self.backend = backend or CudaBackend(num_experts, top_k, hidden_size, intermediate_size, pool.dtype,
                                               pool.device, renormalize)
 
@@ -124,6 +222,8 @@ class ExpertParallelMoE:
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of this layer")
         G, C = self.G, self.C
+        if self.transport is not None:
+            return self.backend.layer(x, router_logits, G, C, self.pool, self.pages, self.E_loc)
         # routing + gather into [G][1 header + C payload rows][H]; the headers carry the
         # per-expert counts, so one all-to-all moves counts and rows together
         send, state = self.backend.dispatch(x, router_logits, G, C)
@@ -139,3 +239,9 @@ class ExpertParallelMoE:
         return self.backend.combine(back, state, T, G, C)
 
     __call__ = forward
+
+    def close(self):
+        """Release the exchange arenas of the p2p transport (collective)."""
+        if self.transport is not None:
+            self.transport.close()
+            self.transport = None

@@ -584,8 +584,10 @@ def bench_verify_step(dev, stream, hbm_peak, steps: int = 5):
 def run_ep(args, cfg, rank, world, dev):
     """N > 1: expert parallelism, strong scaling.  One verify batch of T tokens per step is
     spread over the N ranks (T/N each); rank r holds experts [r*E/N, (r+1)*E/N); rows are
-    dispatched and returned with fixed-capacity NCCL all-to-alls (ae_b200/ep.py), with no
-    host synchronisation, so the step is replayed from a CUDA graph."""
+    dispatched and returned by the kernels over peer memory (the default, ``--ep-transport
+    p2p``) or with fixed-capacity NCCL all-to-alls (``nccl``), with no host synchronisation
+    either way, so the step is replayed from a CUDA graph (ae_b200/ep.py).  The other
+    transport is timed on the same ranks for comparison."""
     import torch.distributed as dist
     from ae_b200 import configs
     from ae_b200.ep import ExpertParallelMoE
@@ -598,7 +600,7 @@ def run_ep(args, cfg, rank, world, dev):
     T_r = cfg.T // world
     pool = configs.make_pool(cfg, dev, seed=0, experts=range(rank * E_loc, (rank + 1) * E_loc))
     x, logits = configs.make_inputs(cfg, dev, seed=rank, T=T_r)
-    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r)
+    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r, transport=args.ep_transport)
 
     def step():
         return moe(x, logits)
@@ -609,7 +611,10 @@ def run_ep(args, cfg, rank, world, dev):
         step()
     torch.cuda.synchronize(dev)
     eager = timed_steps(step, args.steps, stream)
-    mode = "cuda_graph (one expert-parallel layer call per replay, NCCL inside the graph)"
+    mode = ("cuda_graph (one expert-parallel layer call per replay: rows moved by the kernels over peer "
+            "memory, no collective)" if args.ep_transport == "p2p" else
+            "cuda_graph (one expert-parallel layer call per replay, NCCL inside the graph)")
+    graph = None
     try:
         graph = graph_of(step, dev)
         run = graph.replay
@@ -636,6 +641,26 @@ def run_ep(args, cfg, rank, world, dev):
     elapsed, eager = float(el[0].item()), float(el[1].item())
     clocks = sampler.summary(t_soak, t_end)
     sampler.stop()
+
+    # the same layer with the other transport, graph replays, max over ranks
+    other = "nccl" if args.ep_transport == "p2p" else "p2p"
+    moe2 = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r, transport=other)
+
+    def step2():
+        return moe2(x, logits)
+
+    for _ in range(3):
+        step2()
+    g2 = graph_of(step2, dev)
+    for _ in range(3):
+        g2.replay()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t2 = torch.tensor([timed_steps(g2.replay, args.steps, stream) / args.steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    del g2
+    torch.cuda.synchronize(dev)
+    moe2.close()
 
     # the local expert FFN of a step on the rows this rank received, replayed from a
     # graph and timed alone (the dominant work of a rank)
@@ -679,6 +704,9 @@ def run_ep(args, cfg, rank, world, dev):
     t = torch.tensor([e2e_el], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_el = float(t.item())
+    del graph
+    torch.cuda.synchronize(dev)
+    moe.close()
     if rank != 0:
         return
     step_s = elapsed / args.steps
@@ -714,7 +742,8 @@ def run_ep(args, cfg, rank, world, dev):
         "e2e": {"value": round(cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
                 "h2d_bytes_per_step": world * (x.numel() * x.element_size() + logits.numel() * logits.element_size()),
                 "d2h_bytes_per_step": world * x.numel() * x.element_size(),
-                "api": "ae_b200.ep.ExpertParallelMoE.forward"},
+                "api": f"ae_b200.ep.ExpertParallelMoE.forward (transport={args.ep_transport})"},
+        f"{other}_transport_us_per_layer": round(float(t2.item()) * 1e6, 2),
         "gpu_launches": 5 * args.steps,
         "clocks": clocks,
     }
@@ -754,6 +783,8 @@ def main():
     ap.add_argument("--sweep", type=int, nargs="*", default=[16, 64])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-verify", action="store_true", help="skip the 32-layer verify-step block")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: rows over peer memory by the kernels, or NCCL all-to-alls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

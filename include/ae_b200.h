@@ -163,6 +163,38 @@ SMB_API int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool,
 SMB_API int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int k, int H, int I, int G,
                                int C, const void* ws, size_t ws_bytes, smb_stream_t stream);
 
+/* Expert parallelism over peer memory (NVLink), without a collective library.  Every rank
+ * owns an exchange arena of smb_ep_arena_bytes(G, C, H, dtype) bytes (the same layout on
+ * all ranks) that its peers map through CUDA IPC: smb_ep_ipc_alloc on each rank, the
+ * 64-byte handles exchanged by the host (e.g. torch.distributed), smb_ep_ipc_open of
+ * every peer's handle.  `arenas` is then a host array of G device pointers, arenas[r]
+ * being rank r's arena as seen from this process (this rank's own at index `rank`).
+ * A layer call is the three calls below, in this order, on every rank (a rank without
+ * tokens passes T = 0 and still makes them):
+ *   dispatch: routing, then the rows for rank d are written into d's arena and a flag
+ *     raised there when they have all landed;
+ *   experts: waits (bounded) for the G flags, runs the local experts, writes each row's
+ *     output into its source's arena and raises a flag there;
+ *   combine: waits (bounded) for the G return flags, weighted sum into out [T,H].
+ * Flags carry an epoch kept in the arena (the count of finished calls), so calls can be
+ * replayed from a CUDA graph.  A wait that runs out (2 s) records SMB_ERR_DEVICE_TIMEOUT in
+ * the workspace status (smb_moe_read_status) and the call continues without the missing
+ * rows.  G <= 8.  The reference has no expert-parallel path (see smb_moe_ep_dispatch). */
+SMB_API size_t smb_ep_arena_bytes(int G, int C, int H, int dtype);
+SMB_API int smb_ep_ipc_alloc(size_t bytes, void** dev_ptr, void* ipc_handle /* 64 bytes out */);
+SMB_API int smb_ep_ipc_open(const void* ipc_handle, void** peer_ptr);
+SMB_API int smb_ep_ipc_close(void* peer_ptr);
+SMB_API int smb_ep_ipc_free(void* dev_ptr);
+SMB_API int smb_moe_ep_dispatch_p2p(const void* router_logits, int logits_dtype, const void* x, int dtype, int T,
+                                    int E, int k, int H, int I, int renormalize, int G, int rank, int C,
+                                    void* const* arenas, float* topk_weights, int32_t* topk_ids, void* ws,
+                                    size_t ws_bytes, smb_stream_t stream);
+SMB_API int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const void* pool, int64_t num_pages,
+                                   const int64_t* page_of_expert, int dtype, int E_loc, int H, int I, void* ws,
+                                   size_t ws_bytes, smb_stream_t stream);
+SMB_API int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int I, int G, int rank, int C,
+                                   void* const* arenas, const void* ws, size_t ws_bytes, smb_stream_t stream);
+
 /* Whole layer: route + ffn + combine (FusedMoE.forward, FusedMoE.py:508-532, without
  * the tensor-parallel all-reduce).  out may alias x (the reference writes in place). */
 SMB_API int smb_moe_forward(const void* x, const void* router_logits, int logits_dtype, const void* pool,

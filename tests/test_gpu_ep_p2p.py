@@ -1,0 +1,111 @@
+"""Expert-parallel layer over peer memory (transport="p2p": rows written into the peers'
+IPC-mapped exchange arenas by the kernels, flags instead of a collective) on 2 GPUs,
+against the fp32 CPU oracle; also a rank without tokens, repeated calls (the epoch
+advances) and a CUDA-graph replay.  Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    moe = None
+    try:
+        from ae_b200 import ops
+        from ae_b200.ep import ExpertParallelMoE
+        E, k, H, I = 8, 2, 256, 128
+        g = torch.Generator().manual_seed(7)
+        full = (torch.randn(E, 3 * I * H, generator=g) * 0.05).to(torch.bfloat16)
+        E_loc = E // world
+        pool = full[rank * E_loc:(rank + 1) * E_loc].contiguous().to(dev)
+        moe = ExpertParallelMoE(E, k, H, I, pool, max_tokens=40, transport="p2p")
+        res = []
+        for call, T in enumerate([[40, 23], [0, 17], [31, 40]]):
+            Tr = T[rank]
+            gx = torch.Generator().manual_seed(50 + rank + 10 * call)
+            x = torch.randn(Tr, H, generator=gx).to(torch.bfloat16)
+            logits = torch.randn(Tr, E, generator=gx).to(torch.bfloat16)
+            out = moe(x.to(dev), logits.to(dev)).clone()
+            torch.cuda.synchronize()
+            if Tr:
+                w, ids = mo.select_experts(logits, k, True)
+                ref = mo.stack_fused_moe(x, full, torch.arange(E), w, ids, rounding="fp32")
+                res.append(mo.error_metrics(out.float().cpu(), ref))
+            else:
+                res.append((0.0 if out.shape == (0, H) else 1.0, 0.0))
+        # graph replay of a call (the epoch lives in device memory)
+        gx = torch.Generator().manual_seed(99 + rank)
+        x = torch.randn(32, H, generator=gx).to(torch.bfloat16).to(dev)
+        logits = torch.randn(32, E, generator=gx).to(torch.bfloat16).to(dev)
+        eager = moe(x, logits).clone()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            moe(x, logits)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = moe(x, logits)
+        same = True
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            same = same and bool(torch.equal(out, eager))
+        ws = moe.backend._bufs[("ws_src", 32)]
+        status = ops._status(ws, 32, E, k, H, I, ops.storage_code(torch.bfloat16),
+                             torch.cuda.current_stream(dev).cuda_stream)
+        q.put((rank, res, same, status))
+        del graph
+        dist.barrier()
+    finally:
+        if moe is not None:
+            moe.close()
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_peer_memory_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for _ in range(2):
+        rank, res, same, status = q.get(timeout=5)
+        for call, (max_abs, rel) in enumerate(res):
+            assert max_abs <= 2e-2 and rel <= 1e-2, (rank, call, max_abs, rel)
+        assert same, f"rank {rank}: graph replay differs from the eager call"
+        assert status == 0, f"rank {rank}: device status {status}"
