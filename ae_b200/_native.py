@@ -38,6 +38,9 @@ SIGNATURES = {
     "smb_moe_forward": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_forward_routed": (_I, [_P, _P, _P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
     "smb_moe_forward_noalloc": (_I, [_P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "smb_moe_page_copy": (_I, [_P, _P, _S, _P, _I, _P]),
+    "smb_moe_forward_streamed": (_I, [_P, _P, _I, _P, _L, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P,
+                                      _S, _P]),
     "smb_ep_arena_bytes": (_S, [_I, _I, _I, _I]),
     "smb_ep_ipc_alloc": (_I, [_S, ctypes.POINTER(ctypes.c_void_p), _P]),
     "smb_ep_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),

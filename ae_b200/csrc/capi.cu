@@ -27,6 +27,24 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+typedef CUresult (*StreamWriteValue32Fn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+// cuStreamWriteValue32: a stream-ordered 32-bit write done by the GPU's front end, so a
+// copy stream can raise a flag that a running kernel polls without needing an SM.
+StreamWriteValue32Fn write_value_fn() {
+  static StreamWriteValue32Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<StreamWriteValue32Fn>(p);
+    }
+  });
+  return fn;
+}
+
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
@@ -356,7 +374,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
 // run both phases in one persistent launch.
 int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
            int T, int E, int k, int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases,
-           bool counters_zeroed) {
+           bool counters_zeroed, const int* page_ready = nullptr, int page_epoch = 0) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
@@ -396,6 +414,8 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.H = H;
   args.I = I;
   args.Tk = T * k;
+  args.page_ready = page_ready;
+  args.page_epoch = page_epoch;
   args.splits = L.splits;
   args.phase_mask = phases;
   if (!counters_zeroed) {
@@ -754,6 +774,40 @@ int smb_moe_forward_shared(const void* x, const void* router_logits, int logits_
   rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, Et, kt, H, I, ws, ws_bytes, s, 3, true);
   if (rc != SMB_OK) return rc;
   return do_combine(out, dtype, T, Et, kt, H, I, ws, ws_bytes, s);
+}
+
+int smb_moe_page_copy(void* page_dst, const void* host_src, size_t bytes, int* page_ready, int epoch,
+                      smb_stream_t copy_stream) {
+  if (page_dst == nullptr || host_src == nullptr || page_ready == nullptr) return SMB_ERR_NULL;
+  if (bytes == 0) return SMB_ERR_SHAPE;
+  if (!aligned(page_ready, 4)) return SMB_ERR_ALIGN;
+  StreamWriteValue32Fn wv = write_value_fn();
+  if (wv == nullptr) return SMB_ERR_CUDA;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(copy_stream);
+  cudaError_t err = cudaMemcpyAsync(page_dst, host_src, bytes, cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) return cuda_fail(err);
+  const CUresult r = wv(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(page_ready),
+                        static_cast<cuuint32_t>(epoch), 0);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuStreamWriteValue32 failed (%d)", static_cast<int>(r));
+    return SMB_ERR_CUDA;
+  }
+  return SMB_OK;
+}
+
+int smb_moe_forward_streamed(const void* x, const void* router_logits, int logits_dtype, const void* pool,
+                             int64_t num_pages, const int64_t* page_of_expert, const int* page_ready, int page_epoch,
+                             int dtype, int T, int E, int k, int H, int I, int renormalize, void* out,
+                             float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes, smb_stream_t stream) {
+  if (page_ready == nullptr && T > 0) return SMB_ERR_NULL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = smb_moe_route(router_logits, logits_dtype, x, dtype, T, E, k, H, I, renormalize, topk_weights,
+                         topk_ids, ws, ws_bytes, stream);
+  if (rc != SMB_OK) return rc;
+  rc = do_ffn(x, 0, pool, num_pages, page_of_expert, dtype, T, E, k, H, I, ws, ws_bytes, s, 3, true, page_ready,
+              page_epoch);
+  if (rc != SMB_OK) return rc;
+  return do_combine(out, dtype, T, E, k, H, I, ws, ws_bytes, s);
 }
 
 int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream) {

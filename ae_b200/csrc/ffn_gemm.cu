@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (units are claimed roughly in CTA order, and any CTA reuses what another fetched).
   // A guess only: the prefetch is bounds-checked by the tensor map and never waited on.
   // page_of_expert was written before the router started, so it is final here.
-  if (threadIdx.x == 0 && do1) {
+  if (threadIdx.x == 0 && do1 && args.page_ready == nullptr) {
     const int m1 = (I + 127) / 128;
     const int e = static_cast<int>(blockIdx.x) / m1;
     if (e < E) {
@@ -351,6 +351,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = s_touched[un.te];
         const int page = s_page[un.te];
         const int n_e = args.expert_off[e + 1] - args.expert_off[e];
+        if (args.page_ready != nullptr) {
+          // streamed pages: the weights of this unit's page must have arrived
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_sys(args.page_ready + page) < args.page_epoch) {
+            if (*reinterpret_cast<volatile int*>(&s_abort)) {
+              ok = false;
+              break;
+            }
+            if (global_timer_ns() - t0 > kWaitBudgetNs) {
+              record_status(args.status, kDevTimeout);
+              s_abort = 1;
+              ok = false;
+              break;
+            }
+            __nanosleep(200);
+          }
+          if (!ok) break;
+          // the page was written by the copy engine; the TMA reads it through the async proxy
+          asm volatile("fence.proxy.async;" ::: "memory");
+        }
         const CUtensorMap* map = un.phase == 1 ? &tm_w13 : &tm_w2;
         // rows of the two 128-row boxes
         const int r0 = un.phase == 1 ? page * 3 * I + un.mt * 128 : page * 3 * H + 2 * H + un.mt * 256;

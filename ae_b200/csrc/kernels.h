@@ -44,6 +44,10 @@ struct FfnArgs {
   long long num_pages;            // P
   int E, H, I, Tk, splits;
   int phase_mask;                 // 1: gate/up, 2: down, 3: both in one launch
+  // streamed expert pages: page p's weights are usable once page_ready[p] >= page_epoch
+  // (raised by the copy stream after the page's host-to-device copy); nullptr: resident
+  const int* page_ready;
+  int page_epoch;
 };
 
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,

@@ -57,6 +57,9 @@ class Workspace:
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        device = torch.device(device)
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         key = (device.index, torch.cuda.current_stream(device).cuda_stream)
         with cls._lock:
             buf = cls._bufs.get(key)

@@ -224,6 +224,25 @@ SMB_API int smb_moe_forward_shared(const void* x, const void* router_logits, int
                                    int H, int I, int renormalize, void* out, float* topk_weights, int32_t* topk_ids,
                                    void* ws, size_t ws_bytes, smb_stream_t stream);
 
+/* Expert pages streamed from host memory while the layer runs (the reference keeps the
+ * experts in page-locked host memory and copies them into its GPU page pool per layer:
+ * HtoDTransferEngine / StreamPriorityEngine.decode_load_weight,
+ * specmoe/backend/htod_transfer_engine.py:260-341, specmoe/engine.py:143-154,549-588).
+ * smb_moe_page_copy queues, on copy_stream, the copy of one page (bytes from page-locked
+ * host_src to page_dst, one cudaMemcpyAsync) followed by a write of `epoch` to the device
+ * int page_ready (cuStreamWriteValue32, no kernel involved).  smb_moe_forward_streamed is
+ * smb_moe_forward whose FFN kernel starts at once and waits (bounded) per unit for
+ * page_ready[page] >= page_epoch before it loads that page's weights, so experts are
+ * computed while later pages are still crossing PCIe.  page_ready holds one int per page of
+ * the pool (num_pages), starts at 0; use a larger epoch for every new round of copies. */
+SMB_API int smb_moe_page_copy(void* page_dst, const void* host_src, size_t bytes, int* page_ready, int epoch,
+                              smb_stream_t copy_stream);
+SMB_API int smb_moe_forward_streamed(const void* x, const void* router_logits, int logits_dtype, const void* pool,
+                                     int64_t num_pages, const int64_t* page_of_expert, const int* page_ready,
+                                     int page_epoch, int dtype, int T, int E, int k, int H, int I, int renormalize,
+                                     void* out, float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes,
+                                     smb_stream_t stream);
+
 /* Zero the workspace's control block (its first 256 bytes).  Call once after allocating
  * a workspace, before its first smb_moe_forward_gated call: the gated launch counts its
  * CTAs in a ticket kept there, and every call leaves the ticket at 0 again. */

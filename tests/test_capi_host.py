@@ -121,3 +121,9 @@ def test_specmoe_shim_routes_reference_imports():
                 sys.modules.pop(k, None)
             else:
                 sys.modules[k] = v
+
+
+def test_page_streamer_needs_pinned_host_pages():
+    from ae_b200.streaming import ExpertPageStreamer
+    with pytest.raises(ValueError):
+        ExpertPageStreamer(torch.zeros(2, 3 * 64 * 128, dtype=torch.bfloat16), 2, "cpu")
