@@ -127,3 +127,17 @@ def test_page_streamer_needs_pinned_host_pages():
     from ae_b200.streaming import ExpertPageStreamer
     with pytest.raises(ValueError):
         ExpertPageStreamer(torch.zeros(2, 3 * 64 * 128, dtype=torch.bfloat16), 2, "cpu")
+
+
+def test_exchange_arena_layout(lib):
+    """Arena of the peer-memory transport: 1 KiB control + flag block, then recv [G][C+1][H]
+    and back [G][C][H], each rounded up to 256 bytes; at most 8 ranks."""
+    def up(v):
+        return (v + 255) // 256 * 256
+    for G, C, H in [(2, 64, 4096), (8, 64, 4096), (4, 17, 128)]:
+        want = 1024 + up(G * (C + 1) * H * 2) + up(G * C * H * 2)
+        assert lib.smb_ep_arena_bytes(G, C, H, 1) == want
+    assert lib.smb_ep_arena_bytes(9, 64, 4096, 1) == 0
+    assert lib.smb_ep_arena_bytes(2, 64, 4096, 7) == 0
+    assert lib.smb_ep_ipc_alloc(0, None, None) == -8
+    assert lib.smb_moe_page_copy(None, None, 16, None, 1, None) == -8
