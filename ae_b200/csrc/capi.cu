@@ -392,8 +392,11 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   if (!di.sm100) return SMB_ERR_ARCH;
   const bool bf16 = dtype == SMB_DTYPE_BF16;
 
-  CUtensorMap w13, w2;
+  CUtensorMap w13, w2, txp, ta2;
   if ((rc = encode_2d(&w13, pool, dtype, rows1, H, 128)) != SMB_OK) return rc;
+  // token-row tiles for wide experts: the workspace's xp [rows, H] and a2 [rows, I]
+  if ((rc = encode_2d(&txp, at<void>(ws, L.xp), dtype, L.rows, H, 64)) != SMB_OK) return rc;
+  if ((rc = encode_2d(&ta2, at<void>(ws, L.a2), dtype, L.rows, I, 64)) != SMB_OK) return rc;
   if ((rc = encode_2d(&w2, pool, dtype, rows2, I, 128)) != SMB_OK) return rc;
 
   FfnArgs args{};
@@ -423,7 +426,7 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
     cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (static_cast<size_t>(E) * L.splits + 2), stream);
     if (err != cudaSuccess) return cuda_fail(err);
   }
-  cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, args);
+  cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, txp, ta2, args);
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 

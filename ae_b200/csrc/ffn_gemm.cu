@@ -71,7 +71,14 @@ constexpr int kQueue = 8;                      // unit-id queue between the prod
 constexpr int kQueueReaders = 2 + kLoaderWarps;  // MMA thread, each loader-warp leader, epilogue leader
 constexpr int kDynSmem = 227 * 1024 - 4096;  // static shared block (~3.5 KB) + this <= 227 KB
 constexpr int kEpiStage = 4 * 2048;            // epilogue staging, 2 KB per epilogue warp, at the end
-constexpr int kPrefetchBlocks = 16;            // K blocks of the first unit warmed in L2 (512 KB)
+constexpr int kPrefetchBlocks = 16;
+#ifndef SMB_TMA_B_MIN
+#define SMB_TMA_B_MIN 128
+#endif
+// Token tiles at least this wide (after rounding to 64 rows) come by TMA (64-row boxes)
+// instead of cp.async: at 128+ tokens per expert the loader warps' cp.async stream fell
+// behind the MMA.
+constexpr int kTmaBMin = SMB_TMA_B_MIN;            // K blocks of the first unit warmed in L2 (512 KB)
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -163,6 +170,7 @@ __device__ __forceinline__ int split_need(const Geometry& g, int ks) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     ffn_gemm_kernel(const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_w2,
+                    const __grid_constant__ CUtensorMap tm_xp, const __grid_constant__ CUtensorMap tm_a2,
                     const FfnArgs args) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t dyn_smem[];
@@ -258,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     int ncap = (maxn + 15) & ~15;
     ncap = max(16, min(kMaxN, ncap));
+    if (ncap >= kTmaBMin) ncap = min(kMaxN, (ncap + 63) & ~63);  // whole 64-row TMA boxes
     const int stage_bytes = kATileBytes + ncap * 128;
     s_ntouched = nt;
     s_ncap = ncap;
@@ -299,6 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nstages = s_stages;
   const int stage_bytes = kATileBytes + ncap * 128;
   const int nbuf = ncap <= 128 ? 2 : 1;
+  const bool tma_b = ncap >= kTmaBMin;
   const uint32_t acc1_off = nbuf == 2 ? 128u : 256u;
 
   Geometry g;
@@ -503,6 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ready = __shfl_sync(full, ready, 0);
         if (!ready) break;
+        if (tma_b && lane == 0) asm volatile("fence.proxy.async;" ::: "memory");
       }
       for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
         const int nlen = min(ncap, n_e - n0);
@@ -530,6 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          // xp was written by generic stores; a TMA token load reads it through the async proxy
+          if (tma_b && lane == 0) asm volatile("fence.proxy.async;" ::: "memory");
           gathered = true;
         }
         const T* src = un.phase == 1 ? xp : a2;
@@ -542,15 +555,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t sB = ring_base + stage * stage_bytes + kATileBytes;
-          // nb rows x 8 chunks of 16 B, written with the 128-byte swizzle (chunk ^ row%8)
-          for (int c = bt; c < nb * 8; c += kLoaderThreads) {
-            const int r = c >> 3;
-            const int q = c & 7;
-            const bool valid = r < nlen;
-            const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
-            cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid, pol_rows);
+          if (tma_b) {
+            // one thread loads ceil(nb / 64) boxes of 64 rows (same swizzled layout); the
+            // other loader threads only arrive.  Rows past the expert's tokens belong to
+            // the next expert (or are zero past the buffer) and are never stored.
+            if (bt == 0) {
+              const int boxes = (nb + 63) / 64;
+              mbar_arrive_expect_tx(&fullB_bar[stage], static_cast<uint32_t>(boxes) * 64u * 128u);
+              const CUtensorMap* mb = un.phase == 1 ? &tm_xp : &tm_a2;
+              for (int j = 0; j < boxes; ++j) {
+                tma_load_2d(dyn_smem + (sB - raw_base) + j * 64 * 128, mb, &fullB_bar[stage], kb * kBK,
+                            row0 + n0 + j * 64, pol_rows);
+              }
+            } else {
+              mbar_arrive(&fullB_bar[stage]);
+            }
+          } else {
+            // nb rows x 8 chunks of 16 B, written with the 128-byte swizzle (chunk ^ row%8)
+            for (int c = bt; c < nb * 8; c += kLoaderThreads) {
+              const int r = c >> 3;
+              const int q = c & 7;
+              const bool valid = r < nlen;
+              const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
+              cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid, pol_rows);
+            }
+            cp_async_arrive_noinc(&fullB_bar[stage]);
           }
-          cp_async_arrive_noinc(&fullB_bar[stage]);
           if (++stage == nstages) {
             stage = 0;
             phase ^= 1u;
@@ -562,7 +592,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;          // TMEM lane quarter this warp may read
-    const int row = sub * 32 + lane;   // accumulator row = TMEM lane
     const int et = threadIdx.x - 32 * kEpiWarp0;  // 0..127
     // A2 rows are read back by the down units and the partials by the combine moments
     // later; keep them in L2 while the weight stream (evict-first) passes through
@@ -686,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- host side
 
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
-                            const CUtensorMap& w2, const FfnArgs& args) {
+                            const CUtensorMap& w2, const CUtensorMap& xp, const CUtensorMap& a2, const FfnArgs& args) {
   static std::atomic<int> seen_bf16[64], seen_f16[64];
   const void* fn = bf16 ? reinterpret_cast<const void*>(&ffn_gemm_kernel<__nv_bfloat16>)
                         : reinterpret_cast<const void*>(&ffn_gemm_kernel<__half>);
@@ -702,7 +731,8 @@ cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, 
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* params[] = {const_cast<CUtensorMap*>(&w13), const_cast<CUtensorMap*>(&w2), const_cast<FfnArgs*>(&args)};
+  void* params[] = {const_cast<CUtensorMap*>(&w13), const_cast<CUtensorMap*>(&w2), const_cast<CUtensorMap*>(&xp),
+                    const_cast<CUtensorMap*>(&a2), const_cast<FfnArgs*>(&args)};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

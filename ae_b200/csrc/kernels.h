@@ -51,7 +51,7 @@ struct FfnArgs {
 };
 
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
-                            const CUtensorMap& w2, const FfnArgs& args);
+                            const CUtensorMap& w2, const CUtensorMap& xp, const CUtensorMap& a2, const FfnArgs& args);
 
 // Expert-parallel exchange over peer memory.  Rank r's arena (same layout on every rank,
 // mapped by its peers through CUDA IPC) holds a control block (epoch, CTA tickets), the

@@ -803,6 +803,44 @@ def run_ep(args, cfg, rank, world, dev):
     emit(line)
 
 
+def run_ep_rank(args, cfg, dev):
+    """Diagnostic (``--ep-rank G``): one rank's share of a G-rank expert-parallel layer call
+    on this GPU, with local buffers instead of peers (for profiling; no metric line): the
+    dispatch of T/G tokens, the local experts on a receive buffer built from G sources'
+    chunks for this rank, and the final combine, each timed from graph replays."""
+    from ae_b200 import configs
+    from ae_b200.ep import CudaBackend
+    G = args.ep_rank
+    E_loc, T_r = cfg.E // G, cfg.T // G
+    C = T_r * cfg.k
+    pool = configs.make_pool(cfg, dev, seed=0, experts=range(0, E_loc))
+    pages = torch.arange(E_loc, device=dev, dtype=torch.int64)
+    b = CudaBackend(cfg.E, cfg.k, cfg.H, cfg.I, torch.bfloat16, dev)
+    recv = torch.zeros(G * (C + 1), cfg.H, dtype=torch.bfloat16, device=dev)
+    for src in range(G):
+        xs, ls = configs.make_inputs(cfg, dev, seed=src, T=T_r)
+        send, _ = b.dispatch(xs, ls, G, C)
+        recv[src * (C + 1):(src + 1) * (C + 1)] = send[0:C + 1]
+    x, lg = configs.make_inputs(cfg, dev, seed=0, T=T_r)
+    send, state = b.dispatch(x, lg, G, C)
+    back = torch.zeros(G * C, cfg.H, dtype=torch.bfloat16, device=dev)
+    steps = {"dispatch": lambda: b.dispatch(x, lg, G, C),
+             "experts": lambda: b.experts(recv, G, C, pool, pages, E_loc),
+             "combine": lambda: b.combine(back, state, T_r, G, C)}
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for name, fn in steps.items():
+        for _ in range(3):
+            fn()
+        gr = graph_of(fn, dev)
+        for _ in range(3):
+            gr.replay()
+        res[name + "_us"] = round(timed_steps(gr.replay, args.steps, stream) / args.steps * 1e6, 2)
+    hdr = recv.view(G, C + 1, cfg.H)[:, 0].contiguous().view(torch.int32)[:, :E_loc]
+    res["rows_received"] = int(hdr.sum())
+    emit({"ep_rank_emulation": {"workload": cfg.name, "ranks": G, "experts_per_rank": E_loc, **res}})
+
+
 _JSON_OUT = None
 
 
@@ -836,6 +874,8 @@ def main():
     ap.add_argument("--sweep", type=int, nargs="*", default=[16, 64])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-verify", action="store_true", help="skip the 32-layer verify-step block")
+    ap.add_argument("--ep-rank", type=int, default=0,
+                    help="diagnostic: time one rank's kernels of a G-rank expert-parallel call on this GPU")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-alls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -858,6 +898,9 @@ def main():
         build.build()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.ep_rank > 0:
+        run_ep_rank(args, cfg, dev)
+        return
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
