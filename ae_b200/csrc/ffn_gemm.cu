@@ -17,17 +17,21 @@
 //   phase 2 unit (expert, 256 hidden rows, K split): rows 2H.. of the page viewed as
 //     [P*3H, I] (the reference's w2_off) against the expert's A2 rows -> fp32 partials
 //     part[split][p][h].
-// A phase-2 unit of expert e needs every phase-1 unit of e: phase-1 epilogues count
-// their finished units per expert (release), the token loaders of phase 2 wait for the
-// count (acquire, bounded).  Every CTA runs its phase-1 units before its phase-2 units
-// and the grid is at most one CTA per SM, so the waits end.
+// A phase-2 unit of expert e and split s needs the phase-1 units of e whose features lie
+// in the split's K range: phase-1 epilogues count their finished units per (expert,
+// split) (release), the token loaders of phase 2 wait for the count (acquire, bounded).
+// Units are claimed in order (all phase-1 units first) and the grid is at most one CTA
+// per SM, so the waits end.
 //
 // Data movement.  Each SM's TMA engine delivers about 50 GB/s; 148 SMs together
 // saturate HBM only if TMA moves nothing but weights.  So weights come by TMA in 16 KB
 // boxes (128 rows x 64 K, 128-byte swizzle, evict-first) and the small, L2-resident token
-// tiles come by cp.async from six loader warps, written in the same swizzled layout.  The
+// tiles come by cp.async from six loader warps, written in the same swizzled layout
+// (tiles of 128+ rows, prefill-sized batches, by TMA in 64-row boxes instead).  The
 // gate/up token rows are first gathered into expert-major order by all CTAs in the
 // prologue (a grid counter tells the loaders when it is complete), the down rows are A2.
+// With streamed expert pages the producer also waits (bounded) for a unit's page to have
+// arrived from host memory before loading it.
 //
 // Roles (384 threads, one CTA per SM):
 //   warp 0      TMA producer (one thread): weight boxes, 32 KB per stage
