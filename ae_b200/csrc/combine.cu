@@ -88,9 +88,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   // each source
   if (a.link.p2p) {
     __shared__ int s_last;
-    if (last_cta_of_grid(a.link.ctrl + 2, &s_last)) {
+    if (last_cta_of_grid(a.link.ctrl + 2, &s_last) && threadIdx.x == 0) {
       const int epoch = a.link.ctrl[0] + 1;
-      for (int s = threadIdx.x; s < a.link.nranks; s += kCombineThreads) st_release_sys(a.link.flag[s], epoch);
+      for (int s = 0; s < a.link.nranks; ++s) st_release_sys(a.link.flag[s], epoch);
     }
   }
 }

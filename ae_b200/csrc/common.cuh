@@ -52,22 +52,24 @@ __device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, int epoc
 }
 
 // Called by every thread of every CTA once its global / peer stores are issued: true in
-// the CTA that finished last (its stores and all others' are then visible system-wide);
-// that CTA leaves the ticket at 0 for the next launch.  No CTA waits for another.
+// the CTA that finished last; that CTA leaves the ticket at 0 for the next launch.  After
+// the CTA barrier one thread fences at system scope (cumulative over the stores of the
+// CTA it has synchronised with) and takes the ticket; in the last CTA that thread fences
+// again, so when it then raises flags every CTA's stores are visible system-wide.  Only
+// thread 0 of the last CTA may raise flags.  No CTA waits for another.
 __device__ __forceinline__ bool last_cta_of_grid(int* ticket, int* s_flag) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int n = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
     *s_flag = atomicAdd(ticket, 1) == n - 1 ? 1 : 0;
+    if (*s_flag) {
+      __threadfence_system();
+      *ticket = 0;
+    }
   }
   __syncthreads();
-  const bool last = *s_flag != 0;
-  if (last) {
-    __threadfence_system();
-    if (threadIdx.x == 0) *ticket = 0;
-  }
-  return last;
+  return *s_flag != 0;
 }
 
 __device__ __forceinline__ void record_status(int* status, int code) {

@@ -386,9 +386,9 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   // destination that this rank's chunk for the current call is complete
   if (a.link.p2p) {
     __shared__ int s_last;
-    if (last_cta_of_grid(a.link.ctrl + 1, &s_last)) {
+    if (last_cta_of_grid(a.link.ctrl + 1, &s_last) && tid == 0) {
       const int epoch = a.link.ctrl[0] + 1;
-      for (int d = tid; d < a.link.nranks; d += kRouteThreads) st_release_sys(a.link.flag[d], epoch);
+      for (int d = 0; d < a.link.nranks; ++d) st_release_sys(a.link.flag[d], epoch);
     }
   }
 }
