@@ -79,9 +79,9 @@ constexpr int kPrefetchBlocks = 16;
 #ifndef SMB_TMA_B_MIN
 #define SMB_TMA_B_MIN 128
 #endif
-// Token tiles at least this wide (after rounding to 64 rows) come by TMA (64-row boxes)
-// instead of cp.async: at 128+ tokens per expert the loader warps' cp.async stream fell
-// behind the MMA.
+// Token tiles of experts with at least this many tokens in the pass come by TMA (64-row
+// boxes) instead of cp.async: at 128+ tokens per expert the loader warps' cp.async stream
+// fell behind the MMA.  Narrower experts of the same launch keep cp.async.
 constexpr int kTmaBMin = SMB_TMA_B_MIN;            // K blocks of the first unit warmed in L2 (512 KB)
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -559,7 +559,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t sB = ring_base + stage * stage_bytes + kATileBytes;
-          if (tma_b) {
+          // per unit: a wide expert's tile by TMA, a narrow one (a few tokens) by cp.async of
+          // just its rows; both give the barrier the same 192 arrivals
+          if (tma_b && nb >= kTmaBMin) {
             // one thread loads ceil(nb / 64) boxes of 64 rows (same swizzled layout); the
             // other loader threads only arrive.  Rows past the expert's tokens belong to
             // the next expert (or are zero past the buffer) and are never stored.
