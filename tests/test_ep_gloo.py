@@ -119,3 +119,30 @@ def test_expert_parallel_matches_single_process(world, tokens):
     res = dict(q.get(timeout=5) for _ in range(world))
     for r in range(world):
         assert res[r] < 1e-4, (r, res[r])
+
+
+def _single_rank_group():
+    if not dist.is_initialized():
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(_free_port())
+        dist.init_process_group("gloo", rank=0, world_size=1)
+
+
+def test_expert_parallel_argument_checks():
+    """Checks that run before any device work: transport names, a backend with the p2p
+    transport, experts that do not shard over the ranks, pool shapes, too many tokens."""
+    from ae_b200.ep import ExpertParallelMoE
+    _single_rank_group()
+    E, k, H, I = 4, 2, 16, 8
+    pool = torch.zeros(E, 3 * I * H)
+    with pytest.raises(ValueError):
+        ExpertParallelMoE(E, k, H, I, pool, max_tokens=4, transport="tcp")
+    with pytest.raises(ValueError):
+        ExpertParallelMoE(E, k, H, I, pool, max_tokens=4, transport="p2p", backend=OracleBackend(E, k, H, I))
+    with pytest.raises(ValueError):
+        ExpertParallelMoE(E, k, H, I, torch.zeros(E, 3 * I * H + 1), max_tokens=4, backend=OracleBackend(E, k, H, I))
+    moe = ExpertParallelMoE(E, k, H, I, pool, max_tokens=4, backend=OracleBackend(E, k, H, I))
+    with pytest.raises(ValueError):
+        moe(torch.zeros(5, H), torch.zeros(5, E))
+    out = moe(torch.zeros(3, H), torch.zeros(3, E))
+    assert out.shape == (3, H)
