@@ -1,7 +1,7 @@
-"""Source guards (CPU): the repository's code must not name a TMA or bulk load with cluster
-multicast, nor the batched host-device copy calls, anywhere (comments included); runs on
-several GPUs are refused while a travelling source file does.  The patterns are built from
-pieces so that this file does not name them either."""
+"""Source guards (CPU): the repository's code must not name the cluster-wide TMA or bulk
+load variants, nor the batched host-device copy calls, anywhere (comments included); runs
+on several GPUs are refused while a travelling source file does.  The patterns are built
+from pieces so that this file does not name them either."""
 import os
 import re
 
