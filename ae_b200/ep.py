@@ -184,6 +184,11 @@ class ExpertParallelMoE:
     reserves ``max_tokens * top_k`` payload rows, the worst case, plus one header row of
     counts, so no count ever has to reach the host and nothing can overflow.  A layer
     call is free of host synchronisation and can be captured in a CUDA graph.
+
+    Buffers are allocated on the first call with a given token count and kept (a captured
+    graph keeps pointing at them): the returned [T, H] tensor is such a buffer and the next
+    call with the same T overwrites it (clone it to keep it), and a caller that uses many
+    different token counts holds one workspace per count.
     """
 
     def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
