@@ -25,6 +25,7 @@ SIGNATURES = {
     "smb_last_cuda_error": (ctypes.c_char_p, []),
     "smb_moe_workspace_bytes": (_S, [_I, _I, _I, _I, _I, _I]),
     "smb_moe_splits": (_I, [_I, _I, _I, _I]),
+    "smb_moe_gate_up_slices": (_I, [_I, _I, _I, _I]),
     "smb_moe_route": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
     "smb_moe_permute": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_ffn": (_I, [_P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
@@ -46,6 +47,7 @@ SIGNATURES = {
     "smb_ep_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "smb_ep_ipc_close": (_I, [_P]),
     "smb_ep_ipc_free": (_I, [_P]),
+    "smb_ep_arena_reset": (_I, [_P, _I, _I, _I, _I, _P]),
     "smb_moe_ep_dispatch_p2p": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "smb_moe_ep_experts_p2p": (_I, [_I, _I, _I, _P, _P, _L, _P, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_ep_combine_p2p": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _S, _P]),
@@ -57,7 +59,21 @@ SIGNATURES = {
     "smb_moe_align_block_size": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "smb_moe_topk": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "smb_moe_read_status": (_I, [_P, _S, _I, _I, _I, _I, _I, _I, _P]),
+    "smb_moe_read_timers": (_I, [_P, _S, _I, _P, _P]),
+    "smb_moe_noalloc_read_status": (_I, [_P]),
 }
+
+
+class Timers(ctypes.Structure):
+    """``smb_timers_t`` of ``include/ae_b200.h``: device-side kernel timers of a workspace."""
+
+    _fields_ = [("ffn_ns", ctypes.c_uint64), ("recv_wait_ns", ctypes.c_uint64),
+                ("combine_wait_ns", ctypes.c_uint64), ("ffn_launches", ctypes.c_uint32),
+                ("recv_waits", ctypes.c_uint32), ("combine_waits", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
+
+    def as_dict(self):
+        return {f[0]: int(getattr(self, f[0])) for f in self._fields_ if f[0] != "reserved"}
 
 _lock = threading.Lock()
 _lib = None

@@ -48,8 +48,13 @@ C4_LAYER = dataclasses.replace(C2_T16, name="C4 Mixtral-8x7B verify layer 4x32 d
 C5 = MoEConfig("C5 Mixtral-8x22B H6144 I16384 E8 k2 T512", 6144, 16384, 8, 2, 512,
                router_std=0.1 / math.sqrt(6144))
 
+# prefill-sized batches through the same Mixtral-8x7B layer (tensor-core bound: 256+
+# tokens per expert)
+C2_T1024 = dataclasses.replace(C2_T16, name="C2 Mixtral-8x7B H4096 I14336 E8 k2 T1024 (prefill-sized)", T=1024)
+C2_T2048 = dataclasses.replace(C2_T16, name="C2 Mixtral-8x7B H4096 I14336 E8 k2 T2048 (prefill-sized)", T=2048)
+
 BY_KEY = {"c1": C1, "c2-16": C2_T16, "c2-64": C2_T64, "c2-256": C2_T256, "c3": C3, "c4": C4_LAYER,
-          "c5": C5}
+          "c5": C5, "c2-1024": C2_T1024, "c2-2048": C2_T2048}
 
 
 def make_pool(cfg: MoEConfig, device, dtype=torch.bfloat16, seed: int = 0, num_pages: int | None = None,

@@ -112,11 +112,12 @@ int check_shape(int T, int E, int k, int H, int I, int dtype) {
   return SMB_OK;
 }
 
-// choose_splits simulates the unit queue (a few ms for the largest shapes), so its
-// answer is kept per shape.
-int cached_splits(int E, int H, int I, int Tk, int sms) {
+// choose_plan simulates the unit queue (a few ms for the largest shapes), so its answer
+// is kept per shape.
+FfnPlan cached_plan(int E, int H, int I, int Tk, int sms) {
   struct Entry {
-    int E, H, I, Tk, sms, s;
+    int E, H, I, Tk, sms;
+    FfnPlan p;
   };
   constexpr int kSlots = 128;
   static Entry table[kSlots];
@@ -126,27 +127,34 @@ int cached_splits(int E, int H, int I, int Tk, int sms) {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < used; ++i) {
       const Entry& t = table[i];
-      if (t.E == E && t.H == H && t.I == I && t.Tk == Tk && t.sms == sms) return t.s;
+      if (t.E == E && t.H == H && t.I == I && t.Tk == Tk && t.sms == sms) return t.p;
     }
   }
-  const int s = choose_splits(E, H, I, Tk, sms);
+  const FfnPlan p = choose_plan(E, H, I, Tk, sms);
   std::lock_guard<std::mutex> lock(mu);
   const int slot = used < kSlots ? used++ : (next++ % kSlots);
-  table[slot] = Entry{E, H, I, Tk, sms, s};
-  return s;
+  table[slot] = Entry{E, H, I, Tk, sms, p};
+  return p;
 }
 
-int splits_for(int E, int H, int I, int Tk, int* out) {
+// The plan for these sizes on the current device.  SMB_SPLIT_K / SMB_KSPLIT_GATE_UP
+// override S / ks1 (experiments; workspaces must then be sized in the same environment).
+int plan_for(int E, int H, int I, int Tk, FfnPlan* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc != SMB_OK) return rc;
+  FfnPlan p = cached_plan(E, H, I, Tk, di.sms);
   const char* env = std::getenv("SMB_SPLIT_K");
-  int s = cached_splits(E, H, I, Tk, di.sms);
   if (env != nullptr) {
     int v = std::atoi(env);
-    if (v >= 1 && v <= I / 64) s = v;
+    if (v >= 1 && v <= I / 64) p.splits = v;
   }
-  *out = s;
+  env = std::getenv("SMB_KSPLIT_GATE_UP");
+  if (env != nullptr) {
+    int v = std::atoi(env);
+    if (v == 1 || v == 2 || v == 4) p.ks1 = v;
+  }
+  *out = p;
   return SMB_OK;
 }
 
@@ -154,10 +162,10 @@ int splits_for(int E, int H, int I, int Tk, int* out) {
 int carve(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype, WsLayout* L) {
   int rc = check_shape(T, E, k, H, I, dtype);
   if (rc != SMB_OK) return rc;
-  int s = 1;
-  rc = splits_for(E, H, I, T * k, &s);
+  FfnPlan plan;
+  rc = plan_for(E, H, I, T * k, &plan);
   if (rc != SMB_OK) return rc;
-  *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s);
+  *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), plan);
   if (ws == nullptr) return SMB_ERR_NULL;
   if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
   if (ws_bytes < L->total) return SMB_ERR_WORKSPACE;
@@ -337,7 +345,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.ws_ids = at<int32_t>(ws, L.ids);
   a.status = at<int>(ws, L.status);
   a.done = at<int>(ws, L.done);
-  a.done_count = E * L.splits + 2;
+  a.done_count = L.ndone;
   a.ep_send = ep.send;
   a.ep_recv = ep.recv;
   a.ep_G = ep.G;
@@ -403,8 +411,13 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.expert_off = at<int32_t>(ws, L.expert_off);
   args.page_of_expert = page_of_expert;
   args.status = at<int>(ws, L.status);
-  args.done = at<int>(ws, L.done);
-  args.sched = at<int>(ws, L.done) + E * L.splits;
+  args.sched = at<int>(ws, L.done);
+  args.done = args.sched + 2;
+  args.fix = args.done + static_cast<size_t>(E) * L.splits * L.ntc;
+  args.gu = at<float>(ws, L.gu);
+  args.ks1 = L.ks1;
+  args.ntc = L.ntc;
+  args.rows = L.rows;
   args.x = x;
   args.x_chunk = x_chunk;
   args.inv = at<int32_t>(ws, L.inv);
@@ -423,7 +436,7 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.phase_mask = phases;
   if (!counters_zeroed) {
     // standalone call: the router zeroed the counters for the first FFN launch only
-    cudaError_t err = cudaMemsetAsync(args.done, 0, sizeof(int) * (static_cast<size_t>(E) * L.splits + 2), stream);
+    cudaError_t err = cudaMemsetAsync(args.sched, 0, sizeof(int) * static_cast<size_t>(L.ndone), stream);
     if (err != cudaSuccess) return cuda_fail(err);
   }
   cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, txp, ta2, args);
@@ -455,6 +468,24 @@ int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const vo
 
 }  // namespace
 
+namespace smb {
+int record_cuda_error(cudaError_t err) { return cuda_fail(err); }
+// Device status word at `status` as an SMB_* code (synchronous on `stream`).
+int read_status_word(const int* status, cudaStream_t stream) {
+  int h = 0;
+  cudaError_t err = cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess) return cuda_fail(err);
+  switch (h) {
+    case kDevOk: return SMB_OK;
+    case kDevTimeout: return SMB_ERR_DEVICE_TIMEOUT;
+    case kDevBadPage: return SMB_ERR_BAD_PAGE;
+    case kDevBadExpertId: return SMB_ERR_BAD_EXPERT;
+    default: return SMB_ERR_CUDA;
+  }
+}
+}  // namespace smb
+
 extern "C" {
 
 int smb_version(void) { return 100; }
@@ -482,16 +513,23 @@ const char* smb_last_cuda_error(void) { return g_last_cuda_error; }
 
 size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype) {
   if (check_shape(T, E, k, H, I, dtype) != SMB_OK) return 0;
-  int s = 1;
-  if (splits_for(E, H, I, T * k, &s) != SMB_OK) return 0;
-  return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s).total;
+  FfnPlan plan;
+  if (plan_for(E, H, I, T * k, &plan) != SMB_OK) return 0;
+  return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), plan).total;
 }
 
 int smb_moe_splits(int E, int H, int I, int Tk) {
   if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0 || Tk < 0) return SMB_ERR_SHAPE;
-  int s = 1;
-  int rc = splits_for(E, H, I, Tk, &s);
-  return rc == SMB_OK ? s : rc;
+  FfnPlan plan;
+  int rc = plan_for(E, H, I, Tk, &plan);
+  return rc == SMB_OK ? plan.splits : rc;
+}
+
+int smb_moe_gate_up_slices(int E, int H, int I, int Tk) {
+  if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0 || Tk < 0) return SMB_ERR_SHAPE;
+  FfnPlan plan;
+  int rc = plan_for(E, H, I, Tk, &plan);
+  return rc == SMB_OK ? plan.ks1 : rc;
 }
 
 int smb_moe_route(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
@@ -561,6 +599,13 @@ int smb_moe_ep_dispatch(const void* router_logits, int logits_dtype, const void*
   ep.link.nranks = G;
   for (int d = 0; d < G; ++d) {
     ep.link.chunk[d] = static_cast<uint8_t*>(send) + static_cast<size_t>(d) * (C + 1) * H * elem_bytes_of(dtype);
+  }
+  if (T == 0) {
+    // no tokens: the peers must still read zero counts in this rank's header rows
+    if (elem_bytes_of(dtype) == 0) return SMB_ERR_DTYPE;
+    const size_t row = static_cast<size_t>(H) * elem_bytes_of(dtype);
+    cudaError_t err = cudaMemset2DAsync(send, (C + 1) * row, 0, row, G, reinterpret_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? SMB_OK : cuda_fail(err);
   }
   return do_route(router_logits, logits_dtype, nullptr, nullptr, x, dtype, T, E, k, H, I, renormalize, topk_weights,
                   topk_ids, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream), ep);
@@ -633,6 +678,16 @@ int smb_ep_ipc_close(void* peer_ptr) {
 int smb_ep_ipc_free(void* dev_ptr) {
   if (dev_ptr == nullptr) return SMB_ERR_NULL;
   cudaError_t err = cudaFree(dev_ptr);
+  return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+}
+
+int smb_ep_arena_reset(void* arena, int G, int C, int H, int dtype, smb_stream_t stream) {
+  if (arena == nullptr) return SMB_ERR_NULL;
+  if (G < 1 || G > kMaxRanks || C < 1 || H < 128 || elem_bytes_of(dtype) == 0) return SMB_ERR_SHAPE;
+  if (!aligned(arena, kAlign)) return SMB_ERR_ALIGN;
+  const EpArena A = make_ep_arena(G, C, H, elem_bytes_of(dtype));
+  // control block (epoch, CTA tickets) and the flag block, everything before the chunks
+  cudaError_t err = cudaMemsetAsync(arena, 0, A.recv, reinterpret_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -898,23 +953,33 @@ int smb_moe_topk(const void* router_logits, int logits_dtype, int T, int E, int 
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
+int smb_moe_read_timers(const void* ws, size_t ws_bytes, int reset, smb_timers_t* out, smb_stream_t stream) {
+  if (ws == nullptr || out == nullptr) return SMB_ERR_NULL;
+  if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
+  if (ws_bytes < kWsHeaderBytes) return SMB_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  DevTimers h{};
+  const void* src = at<const void>(ws, kTimerOffset);
+  cudaError_t err = cudaMemcpyAsync(&h, src, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err == cudaSuccess && reset) err = cudaMemsetAsync(const_cast<void*>(src), 0, sizeof(h), s);
+  if (err != cudaSuccess) return cuda_fail(err);
+  out->ffn_ns = h.ffn_ns;
+  out->recv_wait_ns = h.recv_wait_ns;
+  out->combine_wait_ns = h.combine_wait_ns;
+  out->ffn_launches = h.ffn_launches;
+  out->recv_waits = h.recv_waits;
+  out->combine_waits = h.combine_waits;
+  out->reserved = 0;
+  return SMB_OK;
+}
+
 int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype,
                         smb_stream_t stream) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
-  int h = 0;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(&h, at<const int>(ws, L.status), sizeof(int), cudaMemcpyDeviceToHost, s);
-  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-  if (err != cudaSuccess) return cuda_fail(err);
-  switch (h) {
-    case kDevOk: return SMB_OK;
-    case kDevTimeout: return SMB_ERR_DEVICE_TIMEOUT;
-    case kDevBadPage: return SMB_ERR_BAD_PAGE;
-    case kDevBadExpertId: return SMB_ERR_BAD_EXPERT;
-    default: return SMB_ERR_CUDA;
-  }
+  return read_status_word(at<const int>(ws, L.status), reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

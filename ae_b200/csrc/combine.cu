@@ -153,8 +153,13 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
   if (link.p2p) {
     // the returned rows are complete once every expert rank raised its flag to this epoch
     if (threadIdx.x == 0) {
+      const uint64_t tw = global_timer_ns();
       s_ok = wait_flags_sys(link.wait_flags, link.nranks, link.ctrl[0] + 1) ? 1 : 0;
-      if (!s_ok && blockIdx.x == 0 && blockIdx.y == 0) record_status(status, kDevTimeout);
+      if (blockIdx.x == 0 && blockIdx.y == 0 && status != nullptr) {
+        if (!s_ok) record_status(status, kDevTimeout);
+        DevTimers* tm = timers_of(status);
+        add_wait_time(&tm->combine_wait_ns, &tm->combine_waits, tw);
+      }
     }
     __syncthreads();
   }

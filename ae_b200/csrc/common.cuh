@@ -76,6 +76,36 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// Timer block of the workspace whose status word is `status` (the control block starts
+// at the status word).
+__device__ __forceinline__ DevTimers* timers_of(int* status) {
+  return reinterpret_cast<DevTimers*>(reinterpret_cast<uint8_t*>(status) + kTimerOffset);
+}
+
+// Add one timed wait (ns since t0) to a (sum, count) pair of the timer block.
+__device__ __forceinline__ void add_wait_time(unsigned long long* sum, unsigned int* count, uint64_t t0) {
+  atomicAdd(sum, static_cast<unsigned long long>(global_timer_ns() - t0));
+  atomicAdd(count, 1u);
+}
+
+// Kernel-duration timer of a grid: every CTA calls begin once (after its dependency
+// wait) and end once (after its last store); the CTA that ends last adds the span from
+// the earliest begin to its end.  One thread per CTA calls them.
+__device__ __forceinline__ void grid_timer_begin(DevTimers* tm) {
+  atomicMax(&tm->ffn_neg_t0, ~0ull - static_cast<unsigned long long>(global_timer_ns()));
+}
+__device__ __forceinline__ void grid_timer_end(DevTimers* tm) {
+  __threadfence();
+  const unsigned int n = gridDim.x * gridDim.y * gridDim.z;
+  if (atomicAdd(&tm->ffn_exit, 1u) == n - 1) {
+    const unsigned long long t1 = global_timer_ns();
+    const unsigned long long t0 = ~0ull - atomicExch(&tm->ffn_neg_t0, 0ull);
+    atomicAdd(&tm->ffn_ns, t1 > t0 ? t1 - t0 : 0ull);
+    atomicAdd(&tm->ffn_launches, 1u);
+    atomicExch(&tm->ffn_exit, 0u);
+  }
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

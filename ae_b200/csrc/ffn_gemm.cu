@@ -73,7 +73,7 @@ constexpr int kMaxStages = 8;
 constexpr int kLoaderThreads = 32 * kLoaderWarps;
 constexpr int kQueue = 8;                      // unit-id queue between the producer and the other roles
 constexpr int kQueueReaders = 2 + kLoaderWarps;  // MMA thread, each loader-warp leader, epilogue leader
-constexpr int kDynSmem = 227 * 1024 - 4096;  // static shared block (~3.5 KB) + this <= 227 KB
+constexpr int kDynSmem = 227 * 1024 - 5120;  // static shared block (~3.5 KB) + this <= 227 KB
 constexpr int kEpiStage = 4 * 2048;            // epilogue staging, 2 KB per epilogue warp, at the end
 constexpr int kPrefetchBlocks = 16;
 #ifndef SMB_TMA_B_MIN
@@ -121,37 +121,66 @@ struct Unit {
   int phase;  // 1 or 2
   int te;     // index into the touched-expert list
   int mt;     // 128-feature tile (phase 1) or 256-row tile of w2 (phase 2)
+  int nt;     // token tile of the expert (ncap tokens each)
+  int kq;     // K slice of a gate/up unit (phase 1)
+  int ks;     // split index (phase 2)
   int kb0;    // first 64-wide K block
   int kb1;    // one past the last K block
-  int ks;     // split index (phase 2)
 };
 
 struct Geometry {
   int n1, n2, total;  // phase-1 units, phase-2 units, all
   int m1, m2;         // tiles per expert
   int kb1_total, kb2_total;
-  int splits;
+  int splits;         // down split-K factor S
+  int ks1;            // gate/up K slices
+  const int* ntp;     // [touched + 1] prefix of token tiles over the touched experts (shared memory)
+  int ntouched;
 };
 
+// Touched expert whose token tiles hold global token tile q: the last te with ntp[te] <= q.
+__device__ __forceinline__ int expert_of_tile(const Geometry& g, int q) {
+  int lo = 0, hi = g.ntouched;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (g.ntp[mid] <= q) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Unit order: all gate/up units, expert by expert, then feature tile, token tile and K
+// slice; then all down units, expert by expert, then split, row tile and token tile.
+// Units that stream the same weight rows for different token tiles are adjacent, so they
+// are claimed at about the same time and the later ones read the rows from L2.
 __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
   Unit r;
   if (u < g.n1) {
+    const int per_tile = g.m1 * g.ks1;  // units per token tile of an expert
     r.phase = 1;
-    r.te = u / g.m1;
-    r.mt = u % g.m1;
+    r.te = expert_of_tile(g, u / per_tile);
+    const int nte = g.ntp[r.te + 1] - g.ntp[r.te];
+    const int v = u - g.ntp[r.te] * per_tile;
+    r.mt = v / (nte * g.ks1);
+    const int q = v - r.mt * nte * g.ks1;
+    r.nt = q / g.ks1;
+    r.kq = q - r.nt * g.ks1;
     r.ks = 0;
-    r.kb0 = 0;
-    r.kb1 = g.kb1_total;
+    r.kb0 = static_cast<int>((static_cast<long long>(g.kb1_total) * r.kq) / g.ks1);
+    r.kb1 = static_cast<int>((static_cast<long long>(g.kb1_total) * (r.kq + 1)) / g.ks1);
   } else {
-    // expert-major like the gate/up units, then split, then row tile: an expert's first
-    // down units read only its first features, whose gate/up units finish first
-    const int v = u - g.n1;
-    const int per_expert = g.m2 * g.splits;
+    // expert-major like the gate/up units, then split: an expert's first down units read
+    // only its first features, whose gate/up units finish first
+    const int per_tile = g.m2 * g.splits;
+    const int v0 = u - g.n1;
     r.phase = 2;
-    r.te = v / per_expert;
-    const int q = v - r.te * per_expert;
-    r.ks = q / g.m2;
-    r.mt = q % g.m2;
+    r.te = expert_of_tile(g, v0 / per_tile);
+    const int nte = g.ntp[r.te + 1] - g.ntp[r.te];
+    const int v = v0 - g.ntp[r.te] * per_tile;
+    r.ks = v / (g.m2 * nte);
+    const int q = v - r.ks * g.m2 * nte;
+    r.mt = q / nte;
+    r.nt = q - r.mt * nte;
+    r.kq = 0;
     r.kb0 = static_cast<int>((static_cast<long long>(g.kb2_total) * r.ks) / g.splits);
     r.kb1 = static_cast<int>((static_cast<long long>(g.kb2_total) * (r.ks + 1)) / g.splits);
   }
@@ -162,11 +191,28 @@ __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
 __device__ __forceinline__ int split_kb0(const Geometry& g, int ks) {
   return static_cast<int>((static_cast<long long>(g.kb2_total) * ks) / g.splits);
 }
-// Gate/up units (128 features = 2 K blocks of the down projection each) a down unit of
-// split ks waits for: those whose features overlap the split's K range.
+// Gate/up feature tiles (128 features = 2 K blocks of the down projection each) a down
+// unit of split ks waits for: those whose features overlap the split's K range.
 __device__ __forceinline__ int split_need(const Geometry& g, int ks) {
   const int b0 = split_kb0(g, ks), b1 = split_kb0(g, ks + 1);
   return min(g.m1, (b1 + 1) / 2) - b0 / 2;
+}
+
+// Bounded wait by one thread until *p >= need (acquire at GPU scope); false after the
+// wait budget or when another role aborted.
+__device__ __forceinline__ bool wait_count(const int* p, int need, int* status, volatile int* abort_flag) {
+  const uint64_t t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (ld_acquire(p) >= need) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitBudgetNs) {
+      record_status(status, kDevTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+    if (++spins > 8) __nanosleep(64);
+  }
 }
 
 }  // namespace
@@ -185,6 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t s_tmem;
   __shared__ int s_touched[kMaxExperts];
   __shared__ int s_page[kMaxExperts];
+  __shared__ int s_ntp[kMaxExperts + 1];
   __shared__ int s_ntouched, s_ncap, s_stages;
   __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed;
 
@@ -197,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool do1 = (args.phase_mask & 1) != 0;
   const bool do2 = (args.phase_mask & 2) != 0;
   const bool chained = do1 && do2;  // phase 2 waits on this launch's phase 1
+  const int ks1 = do1 ? args.ks1 : 1;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -228,19 +276,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // While the router (launched just before) may still run, warm L2 with the first K
-  // blocks of the gate/up unit this CTA's index would get if every expert is touched
-  // (units are claimed roughly in CTA order, and any CTA reuses what another fetched).
-  // A guess only: the prefetch is bounds-checked by the tensor map and never waited on.
-  // page_of_expert was written before the router started, so it is final here.
+  // blocks of the gate/up unit this CTA's index would get if every expert is touched and
+  // has one token tile (units are claimed roughly in CTA order, and any CTA reuses what
+  // another fetched).  A guess only: the prefetch is bounds-checked by the tensor map and
+  // never waited on.  page_of_expert was written before the router started, so it is final.
   if (threadIdx.x == 0 && do1 && args.page_ready == nullptr) {
     const int m1 = (I + 127) / 128;
-    const int e = static_cast<int>(blockIdx.x) / m1;
+    const int unit = static_cast<int>(blockIdx.x);
+    const int e = unit / (m1 * ks1);
+    const int mt = (unit / ks1) % m1;
+    const int kq = unit % ks1;
     if (e < E) {
       const long long pg = args.page_of_expert[e];
       if (pg >= 0 && pg < args.num_pages) {
-        const int r0 = static_cast<int>(pg) * 3 * I + (static_cast<int>(blockIdx.x) % m1) * 128;
-        const int kbs = min(H / kBK, kPrefetchBlocks);
-        for (int kb = 0; kb < kbs; ++kb) {
+        const int r0 = static_cast<int>(pg) * 3 * I + mt * 128;
+        const int kbt = H / kBK;
+        const int kb0 = kbt * kq / ks1;
+        const int kbs = min(kbt * (kq + 1) / ks1 - kb0, kPrefetchBlocks);
+        for (int kb = kb0; kb < kb0 + kbs; ++kb) {
           tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0);
           tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0 + I);
         }
@@ -251,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Everything above touched only this CTA's own shared and tensor memory (and L2
   // hints); the routing results and the token rows come from the router.
   pdl_wait_prior_grids();
+  if (threadIdx.x == 0) grid_timer_begin(timers_of(args.status));
 
   if (threadIdx.x == 0) {
     int nt = 0, maxn = 0;
@@ -271,6 +325,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ncap = (maxn + 15) & ~15;
     ncap = max(16, min(kMaxN, ncap));
     if (ncap >= kTmaBMin) ncap = min(kMaxN, (ncap + 63) & ~63);  // whole 64-row TMA boxes
+    // token tiles per touched expert (ncap tokens each), prefix-summed; never more than
+    // the counters' bound args.ntc (an expert with more than 256 tokens has ncap = 256)
+    s_ntp[0] = 0;
+    for (int t = 0; t < nt; ++t) {
+      const int e = s_touched[t];
+      const int n = args.expert_off[e + 1] - args.expert_off[e];
+      s_ntp[t + 1] = s_ntp[t] + min(args.ntc, (n + ncap - 1) / ncap);
+    }
     const int stage_bytes = kATileBytes + ncap * 128;
     s_ntouched = nt;
     s_ncap = ncap;
@@ -321,8 +383,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   g.kb1_total = H / kBK;
   g.kb2_total = I / kBK;
   g.splits = args.splits;
-  g.n1 = do1 ? s_ntouched * g.m1 : 0;
-  g.n2 = do2 ? s_ntouched * g.m2 * g.splits : 0;
+  g.ks1 = ks1;
+  g.ntp = s_ntp;
+  g.ntouched = s_ntouched;
+  const int tiles = s_ntp[s_ntouched];
+  g.n1 = do1 ? tiles * g.m1 * g.ks1 : 0;
+  g.n2 = do2 ? tiles * g.m2 * g.splits : 0;
   g.total = g.n1 + g.n2;
 
   // Units are handed out dynamically: the producer claims the next unit id from a
@@ -338,6 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       qph ^= 1u;
     }
     return u;
+  };
+  // tokens [n0, n0 + nlen) of touched expert te in the unit's token tile
+  auto tile_tokens = [&](const Unit& un, int& row0, int& n0, int& nlen) {
+    const int e = s_touched[un.te];
+    row0 = args.expert_off[e];
+    n0 = un.nt * ncap;
+    nlen = min(ncap, args.expert_off[e + 1] - row0 - n0);
   };
 
   if (warp == 0) {
@@ -362,9 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (u < 0) break;
         const Unit un = decode(u, g);
-        const int e = s_touched[un.te];
         const int page = s_page[un.te];
-        const int n_e = args.expert_off[e + 1] - args.expert_off[e];
         if (args.page_ready != nullptr) {
           // streamed pages: the weights of this unit's page must have arrived
           const uint64_t t0 = global_timer_ns();
@@ -389,21 +460,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // rows of the two 128-row boxes
         const int r0 = un.phase == 1 ? page * 3 * I + un.mt * 128 : page * 3 * H + 2 * H + un.mt * 256;
         const int r1 = un.phase == 1 ? r0 + I : r0 + 128;
-        for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
-          for (int kb = un.kb0; kb < un.kb1; ++kb) {
-            if (!mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort)) {
-              ok = false;
-              break;
-            }
-            uint8_t* sA = dyn_smem + (ring_base - raw_base) + stage * stage_bytes;
-            mbar_arrive_expect_tx(&fullA_bar[stage], kATileBytes);
-            tma_load_2d(sA, map, &fullA_bar[stage], kb * kBK, r0, pol_w);
-            tma_load_2d(sA + kBoxBytes, map, &fullA_bar[stage], kb * kBK, r1, pol_w);
-            ++issued;
-            if (++stage == nstages) {
-              stage = 0;
-              phase ^= 1u;
-            }
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = dyn_smem + (ring_base - raw_base) + stage * stage_bytes;
+          mbar_arrive_expect_tx(&fullA_bar[stage], kATileBytes);
+          tma_load_2d(sA, map, &fullA_bar[stage], kb * kBK, r0, pol_w);
+          tma_load_2d(sA + kBoxBytes, map, &fullA_bar[stage], kb * kBK, r1, pol_w);
+          ++issued;
+          if (++stage == nstages) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
       }
@@ -423,50 +492,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int u = next_unit(qi, qph);
         if (u < 0) break;
         const Unit un = decode(u, g);
-        const int e = s_touched[un.te];
-        const int n_e = args.expert_off[e + 1] - args.expert_off[e];
-        for (int n0 = 0; ok && n0 < n_e; n0 += ncap, ++pass) {
-          const int nb = (min(ncap, n_e - n0) + 15) & ~15;
-          const uint32_t idesc = idesc_f16(kBF16, 128, nb);
-          const int buf = pass % nbuf;
-          if (!mbar_wait(&tempty_bar[buf], ((pass / nbuf) & 1) ^ 1u, args.status, &s_abort)) {
+        int row0, n0, nlen;
+        tile_tokens(un, row0, n0, nlen);
+        const int nb = (nlen + 15) & ~15;
+        const uint32_t idesc = idesc_f16(kBF16, 128, nb);
+        const int buf = pass % nbuf;
+        if (!mbar_wait(&tempty_bar[buf], ((pass / nbuf) & 1) ^ 1u, args.status, &s_abort)) break;
+        tc_fence_after();
+        const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * 256);
+        const uint32_t acc1 = acc0 + acc1_off;
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+          if (!mbar_wait(&fullA_bar[stage], phase, args.status, &s_abort) ||
+              !mbar_wait(&fullB_bar[stage], phase, args.status, &s_abort)) {
             ok = false;
             break;
           }
+          // the token tile was written by cp.async (generic proxy); the MMA reads it
+          // through the async proxy
+          fence_proxy_async_smem();
           tc_fence_after();
-          const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * 256);
-          const uint32_t acc1 = acc0 + acc1_off;
-          for (int kb = un.kb0; kb < un.kb1; ++kb) {
-            if (!mbar_wait(&fullA_bar[stage], phase, args.status, &s_abort) ||
-                !mbar_wait(&fullB_bar[stage], phase, args.status, &s_abort)) {
-              ok = false;
-              break;
-            }
-            // the token tile was written by cp.async (generic proxy); the MMA reads it
-            // through the async proxy
-            fence_proxy_async_smem();
-            tc_fence_after();
-            const uint32_t a_addr = ring_base + stage * stage_bytes;
-            const uint64_t ad0 = desc_kmajor_sw128(a_addr);
-            const uint64_t ad1 = desc_kmajor_sw128(a_addr + kBoxBytes);
-            const uint64_t bd = desc_kmajor_sw128(a_addr + kATileBytes);
+          const uint32_t a_addr = ring_base + stage * stage_bytes;
+          const uint64_t ad0 = desc_kmajor_sw128(a_addr);
+          const uint64_t ad1 = desc_kmajor_sw128(a_addr + kBoxBytes);
+          const uint64_t bd = desc_kmajor_sw128(a_addr + kATileBytes);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              // +32 bytes along K inside the swizzle row = +2 in the encoded start address
-              const uint32_t acc = (kb > un.kb0 || kk > 0) ? 1u : 0u;
-              umma_f16(acc0, ad0 + 2 * kk, bd + 2 * kk, idesc, acc);
-              umma_f16(acc1, ad1 + 2 * kk, bd + 2 * kk, idesc, acc);
-            }
-            umma_commit(&empty_bar[stage]);
-            ++consumed;
-            if (++stage == nstages) {
-              stage = 0;
-              phase ^= 1u;
-            }
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // +32 bytes along K inside the swizzle row = +2 in the encoded start address
+            const uint32_t acc = (kb > un.kb0 || kk > 0) ? 1u : 0u;
+            umma_f16(acc0, ad0 + 2 * kk, bd + 2 * kk, idesc, acc);
+            umma_f16(acc1, ad1 + 2 * kk, bd + 2 * kk, idesc, acc);
           }
-          if (!ok) break;
-          umma_commit(&tfull_bar[buf]);
+          umma_commit(&empty_bar[stage]);
+          ++consumed;
+          if (++stage == nstages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
+        if (!ok) break;
+        umma_commit(&tfull_bar[buf]);
+        ++pass;
       }
       s_consumed = consumed;
     }
@@ -494,103 +559,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (u < 0) break;
       const Unit un = decode(u, g);
       const int e = s_touched[un.te];
-      const int row0 = args.expert_off[e];
-      const int n_e = args.expert_off[e + 1] - row0;
+      int row0, n0, nlen;
+      tile_tokens(un, row0, n0, nlen);
       const int K = un.phase == 1 ? H : I;
-      if (un.phase == 2 && chained) {
-        // A2 rows of expert e are complete once all its gate/up units have counted in
-        int ready = 0;
-        if (lane == 0) {
-          const uint64_t t0 = global_timer_ns();
-          while (true) {
-            if (ld_acquire(args.done + e * g.splits + un.ks) >= split_need(g, un.ks)) {
-              ready = 1;
-              break;
-            }
-            if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-            if (global_timer_ns() - t0 > kWaitBudgetNs) {
-              record_status(args.status, kDevTimeout);
-              s_abort = 1;
-              break;
-            }
-          }
-        }
-        ready = __shfl_sync(full, ready, 0);
-        if (!ready) break;
-        if (tma_b && lane == 0) asm volatile("fence.proxy.async;" ::: "memory");
-      }
-      for (int n0 = 0; ok && n0 < n_e; n0 += ncap) {
-        const int nlen = min(ncap, n_e - n0);
-        const int nb = (nlen + 15) & ~15;
-        if (un.phase == 1 && !gathered) {
+      const int nb = (nlen + 15) & ~15;
+      int ready = 1;
+      if (lane == 0) {
+        if (un.phase == 2 && chained) {
+          // A2 rows of this token tile are complete once the gate/up tiles covering the
+          // split's K range have counted in
+          ready = wait_count(args.done + (e * g.splits + un.ks) * args.ntc + un.nt, split_need(g, un.ks),
+                             args.status, &s_abort) ? 1 : 0;
+        } else if (un.phase == 1 && !gathered) {
           // every CTA's share of xp must be written before the first gate/up tile
-          int ready = 0;
-          if (lane == 0) {
-            const uint64_t t0 = global_timer_ns();
-            while (true) {
-              if (ld_acquire(args.sched + 1) >= static_cast<int>(gridDim.x)) {
-                ready = 1;
-                break;
-              }
-              if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-              if (global_timer_ns() - t0 > kWaitBudgetNs) {
-                record_status(args.status, kDevTimeout);
-                s_abort = 1;
-                break;
-              }
-            }
-          }
-          ready = __shfl_sync(full, ready, 0);
-          if (!ready) {
-            ok = false;
-            break;
-          }
-          // xp was written by generic stores; a TMA token load reads it through the async proxy
-          if (tma_b && lane == 0) asm volatile("fence.proxy.async;" ::: "memory");
-          gathered = true;
+          ready = wait_count(args.sched + 1, static_cast<int>(gridDim.x), args.status, &s_abort) ? 1 : 0;
         }
-        const T* src = un.phase == 1 ? xp : a2;
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
-          int got = 0;
-          if (lane == 0) got = mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort) ? 1 : 0;
-          got = __shfl_sync(full, got, 0);
-          if (!got) {
-            ok = false;
-            break;
-          }
-          const uint32_t sB = ring_base + stage * stage_bytes + kATileBytes;
-          // per unit: a wide expert's tile by TMA, a narrow one (a few tokens) by cp.async of
-          // just its rows; both give the barrier the same 192 arrivals
-          if (tma_b && nb >= kTmaBMin) {
-            // one thread loads ceil(nb / 64) boxes of 64 rows (same swizzled layout); the
-            // other loader threads only arrive.  Rows past the expert's tokens belong to
-            // the next expert (or are zero past the buffer) and are never stored.
-            if (bt == 0) {
-              const int boxes = (nb + 63) / 64;
-              mbar_arrive_expect_tx(&fullB_bar[stage], static_cast<uint32_t>(boxes) * 64u * 128u);
-              const CUtensorMap* mb = un.phase == 1 ? &tm_xp : &tm_a2;
-              for (int j = 0; j < boxes; ++j) {
-                tma_load_2d(dyn_smem + (sB - raw_base) + j * 64 * 128, mb, &fullB_bar[stage], kb * kBK,
-                            row0 + n0 + j * 64, pol_rows);
-              }
-            } else {
-              mbar_arrive(&fullB_bar[stage]);
+        // rows written by generic stores; a TMA token load reads them through the async proxy
+        if (ready && tma_b) asm volatile("fence.proxy.async;" ::: "memory");
+      }
+      ready = __shfl_sync(full, ready, 0);
+      if (!ready) break;
+      if (un.phase == 1) gathered = true;
+      const T* src = un.phase == 1 ? xp : a2;
+      for (int kb = un.kb0; kb < un.kb1; ++kb) {
+        int got = 0;
+        if (lane == 0) got = mbar_wait(&empty_bar[stage], phase ^ 1u, args.status, &s_abort) ? 1 : 0;
+        got = __shfl_sync(full, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint32_t sB = ring_base + stage * stage_bytes + kATileBytes;
+        // per unit: a wide expert's tile by TMA, a narrow one (a few tokens) by cp.async of
+        // just its rows; both give the barrier the same 192 arrivals
+        if (tma_b && nb >= kTmaBMin) {
+          // one thread loads ceil(nb / 64) boxes of 64 rows (same swizzled layout); the
+          // other loader threads only arrive.  Rows past the expert's tokens belong to
+          // the next expert (or are zero past the buffer) and are never stored.
+          if (bt == 0) {
+            const int boxes = (nb + 63) / 64;
+            mbar_arrive_expect_tx(&fullB_bar[stage], static_cast<uint32_t>(boxes) * 64u * 128u);
+            const CUtensorMap* mb = un.phase == 1 ? &tm_xp : &tm_a2;
+            for (int j = 0; j < boxes; ++j) {
+              tma_load_2d(dyn_smem + (sB - raw_base) + j * 64 * 128, mb, &fullB_bar[stage], kb * kBK,
+                          row0 + n0 + j * 64, pol_rows);
             }
           } else {
-            // nb rows x 8 chunks of 16 B, written with the 128-byte swizzle (chunk ^ row%8)
-            for (int c = bt; c < nb * 8; c += kLoaderThreads) {
-              const int r = c >> 3;
-              const int q = c & 7;
-              const bool valid = r < nlen;
-              const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
-              cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid, pol_rows);
-            }
-            cp_async_arrive_noinc(&fullB_bar[stage]);
+            mbar_arrive(&fullB_bar[stage]);
           }
-          if (++stage == nstages) {
-            stage = 0;
-            phase ^= 1u;
+        } else {
+          // nb rows x 8 chunks of 16 B, written with the 128-byte swizzle (chunk ^ row%8)
+          for (int c = bt; c < nb * 8; c += kLoaderThreads) {
+            const int r = c >> 3;
+            const int q = c & 7;
+            const bool valid = r < nlen;
+            const T* p = valid ? src + static_cast<size_t>(row0 + n0 + r) * K + kb * kBK + q * 8 : src;
+            cp_async_16(sB + r * 128 + ((q ^ (r & 7)) << 4), p, valid, pol_rows);
           }
+          cp_async_arrive_noinc(&fullB_bar[stage]);
+        }
+        if (++stage == nstages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
     }
@@ -602,6 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // A2 rows are read back by the down units and the partials by the combine moments
     // later; keep them in L2 while the weight stream (evict-first) passes through
     const uint64_t pol_keep = policy_evict_last();
+    const size_t gu_slice = static_cast<size_t>(args.rows) * 2 * I;  // floats per gate/up K slice
     int qi = 0;
     uint32_t qph = 0;
     int pass = 0;
@@ -615,80 +646,119 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (u < 0) break;
       const Unit un = decode(u, g);
       const int e = s_touched[un.te];
-      const int row0 = args.expert_off[e];
-      const int n_e = args.expert_off[e + 1] - row0;
-      for (int n0 = 0; n0 < n_e; n0 += ncap, ++pass) {
-        const int nlen = min(ncap, n_e - n0);
-        const int buf = pass % nbuf;
-        if (et == 0) {
-          s_epi_ok = mbar_wait(&tfull_bar[buf], (pass / nbuf) & 1, args.status, &s_abort) ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        ok = s_epi_ok != 0;
-        named_bar_sync(1, 128);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t lane_base =
-            tmem + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(buf * 256);
-        // Each warp stages its 32 rows x 16 tokens in shared memory and writes 16-byte
-        // vectors along the row (8 activations or 4 partials per store) instead of one
-        // element per thread per token.
-        uint8_t* stg = dyn_smem + (kDynSmem - kEpiStage) + sub * 2048;
-        for (int c0 = 0; c0 < nlen; c0 += 16) {
-          float va[16], vb[16];
-          tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
-          tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
-          const int nt = min(16, nlen - c0);
-          if (un.phase == 1) {
-            T* st = reinterpret_cast<T*>(stg);
+      int row0, n0, nlen;
+      tile_tokens(un, row0, n0, nlen);
+      const int buf = pass % nbuf;
+      // a gate/up unit cut into K slices: the last slice adds the others' stored partials
+      const bool slice_store = un.phase == 1 && ks1 > 1 && un.kq < ks1 - 1;
+      const bool slice_sum = un.phase == 1 && ks1 > 1 && un.kq == ks1 - 1;
+      const int fixc = (e * g.m1 + un.mt) * args.ntc + un.nt;  // K-slice counter of this tile
+      if (et == 0) {
+        bool okw = mbar_wait(&tfull_bar[buf], (pass / nbuf) & 1, args.status, &s_abort);
+        if (okw && slice_sum) okw = wait_count(args.fix + fixc, ks1 - 1, args.status, &s_abort);
+        s_epi_ok = okw ? 1 : 0;
+      }
+      named_bar_sync(1, 128);
+      ok = s_epi_ok != 0;
+      named_bar_sync(1, 128);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t lane_base =
+          tmem + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(buf * 256);
+      // Each warp stages its 32 rows x 16 tokens in shared memory and writes 16-byte
+      // vectors along the row (8 activations or 4 partials per store) instead of one
+      // element per thread per token.
+      uint8_t* stg = dyn_smem + (kDynSmem - kEpiStage) + sub * 2048;
+      const int feat = un.mt * 128 + sub * 32 + lane;  // gate/up feature of this thread's TMEM lane
+      for (int c0 = 0; c0 < nlen; c0 += 16) {
+        float va[16], vb[16];
+        tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
+        tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
+        const int nt = min(16, nlen - c0);
+        // this thread's element of token row row0 + n0 + c0 in a gate/up slice [rows, 2I]
+        const size_t gu_at = static_cast<size_t>(row0 + n0 + c0) * 2 * I + feat;
+        const int nrow = feat < I ? nt : 0;
+        if (slice_store) {
+          // fp32 gate and up partial sums of this K slice: lanes of a warp write 32
+          // consecutive features of one token row (128 B) per store
+          float* dst = args.gu + static_cast<size_t>(un.kq) * gu_slice + gu_at;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) st[i * 32 + lane] = from_f32<T>(silu_f32(va[i]) * vb[i]);
+          for (int i = 0; i < 16; ++i) {
+            if (i < nrow) {
+              dst[0] = va[i];
+              dst[I] = vb[i];
+            }
+            dst += 2 * I;
+          }
+        } else if (un.phase == 1) {
+          if (slice_sum) {
+            for (int q = 0; q < ks1 - 1; ++q) {
+              const float* src = args.gu + static_cast<size_t>(q) * gu_slice + gu_at;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (i < nrow) {
+                  va[i] += __ldcg(src);
+                  vb[i] += __ldcg(src + I);
+                }
+                src += 2 * I;
+              }
+            }
+          }
+          T* st = reinterpret_cast<T*>(stg);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) st[i * 32 + lane] = from_f32<T>(silu_f32(va[i]) * vb[i]);
+          __syncwarp();
+#pragma unroll
+          for (int j = lane; j < 64; j += 32) {  // 16 tokens x 4 chunks of 8 features
+            const int i = j >> 2, q = j & 3;
+            const int p = row0 + n0 + c0 + i;
+            const int f = un.mt * 128 + sub * 32 + q * 8;
+            if (i < nt && p >= 0 && p < args.Tk && f < I) {
+              st_evict_last_v4(reinterpret_cast<T*>(args.a2) + static_cast<size_t>(p) * I + f,
+                               *reinterpret_cast<const uint4*>(st + i * 32 + q * 8), pol_keep);
+            }
+          }
+          __syncwarp();
+        } else {
+          float* st = reinterpret_cast<float*>(stg);
+          auto put_rows = [&](const float (&v)[16], int half) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) st[i * 32 + lane] = v[i];
             __syncwarp();
 #pragma unroll
-            for (int j = lane; j < 64; j += 32) {  // 16 tokens x 4 chunks of 8 features
-              const int i = j >> 2, q = j & 3;
+            for (int j = lane; j < 128; j += 32) {  // 16 tokens x 8 chunks of 4 rows
+              const int i = j >> 3, q = j & 7;
               const int p = row0 + n0 + c0 + i;
-              const int f = un.mt * 128 + sub * 32 + q * 8;
-              if (i < nt && p >= 0 && p < args.Tk && f < I) {
-                st_evict_last_v4(reinterpret_cast<T*>(args.a2) + static_cast<size_t>(p) * I + f,
-                                 *reinterpret_cast<const uint4*>(st + i * 32 + q * 8), pol_keep);
+              const int h = un.mt * 256 + half * 128 + sub * 32 + q * 4;
+              if (i < nt && p >= 0 && p < args.Tk && h < H) {
+                st_evict_last_v4(args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H + h,
+                                 *reinterpret_cast<const uint4*>(st + i * 32 + q * 4), pol_keep);
               }
             }
             __syncwarp();
-          } else {
-            float* st = reinterpret_cast<float*>(stg);
-            auto put_rows = [&](const float (&v)[16], int half) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) st[i * 32 + lane] = v[i];
-              __syncwarp();
-#pragma unroll
-              for (int j = lane; j < 128; j += 32) {  // 16 tokens x 8 chunks of 4 rows
-                const int i = j >> 3, q = j & 7;
-                const int p = row0 + n0 + c0 + i;
-                const int h = un.mt * 256 + half * 128 + sub * 32 + q * 4;
-                if (i < nt && p >= 0 && p < args.Tk && h < H) {
-                  st_evict_last_v4(args.part + (static_cast<size_t>(un.ks) * args.Tk + p) * H + h,
-                                   *reinterpret_cast<const uint4*>(st + i * 32 + q * 4), pol_keep);
-                }
-              }
-              __syncwarp();
-            };
-            put_rows(va, 0);
-            put_rows(vb, 1);
-          }
+          };
+          put_rows(va, 0);
+          put_rows(vb, 1);
         }
-        tc_fence_before();
-        mbar_arrive(&tempty_bar[buf]);
       }
-      if (ok && un.phase == 1 && chained) {
-        // publish: this unit's A2 columns are written (release at GPU scope); count it
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[buf]);
+      ++pass;
+      if (slice_store) {
+        // publish this K slice's partials (release at GPU scope) to the tile's last slice
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) atomicAdd(args.fix + fixc, 1);
+      } else if (un.phase == 1 && chained) {
+        // publish: this tile's A2 columns are written (release at GPU scope); count it
         // for every down split whose K range overlaps its 128 features
         __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
           const int f0 = un.mt * 2, f1 = min(un.mt * 2 + 2, g.kb2_total);
           for (int ks = 0; ks < g.splits; ++ks) {
-            if (f0 < split_kb0(g, ks + 1) && f1 > split_kb0(g, ks)) atomicAdd(args.done + e * g.splits + ks, 1);
+            if (f0 < split_kb0(g, ks + 1) && f1 > split_kb0(g, ks))
+              atomicAdd(args.done + (e * g.splits + ks) * args.ntc + un.nt, 1);
           }
         }
       }
@@ -716,6 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (threadIdx.x == 0) grid_timer_end(timers_of(args.status));
 }
 
 // ---------------------------------------------------------------- host side

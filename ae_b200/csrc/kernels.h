@@ -32,8 +32,13 @@ struct FfnArgs {
   const int32_t* expert_off;      // [E+1]
   const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
   int* status;                    // device status word
-  int* done;                      // [E*S] finished gate/up units per (expert, down split), zeroed by the router
-  int* sched;                     // [2] next unit to hand out, CTAs done gathering (zeroed by the router)
+  int* done;                      // [E*S*ntc] finished gate/up tiles per (expert, down split, token tile)
+  int* fix;                       // [E*m1*ntc] gate/up K slices stored per (expert, feature tile, token tile)
+  int* sched;                     // [2] next unit to hand out, CTAs done gathering (all zeroed by the router)
+  float* gu;                      // [ks1-1, rows, 2I] gate/up partials of the K slices before the last
+  int ks1;                        // gate/up K slices (1: none)
+  int ntc;                        // token-tile bound per expert (counter stride)
+  int rows;                       // rows of xp / a2 / each gu slice
   const void* x;                  // token rows: the layer input [T, H], or the exchange layout
   int x_chunk;                    // 0: row t of x; C > 0: payload row t of [G][C+1][H]
   const int32_t* inv;             // [Tk] expert-major position of each flat slot
@@ -137,6 +142,12 @@ cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const floa
                                 int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids = nullptr,
                                 const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1,
                                 const EpLink* link = nullptr, int* status = nullptr);
+
+// Host helpers of the C ABI shared with the other entry-point files: record a CUDA error
+// for smb_last_cuda_error (returns SMB_ERR_CUDA), and read a device status word as an
+// SMB_* code (synchronous on `stream`).
+int record_cuda_error(cudaError_t err);
+int read_status_word(const int* status, cudaStream_t stream);
 
 cudaError_t launch_align(const int32_t* ids, int numel, int E, int block, int32_t* sorted_ids, int32_t* expert_ids,
                          int32_t* num_post_pad, int max_blocks, cudaStream_t stream);

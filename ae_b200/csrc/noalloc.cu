@@ -13,14 +13,16 @@
 //
 // The device address of the array is looked up once per device, on the first call made
 // with that device current (cudaGetSymbolAddress; in host code the array's name is only a
-// host-side stand-in and must never be handed to a kernel).  Make that first call on each
-// device before any stream capture.
+// host-side stand-in and must never be handed to a kernel); a lookup that fails is tried
+// again on the next call.  Make that first call on each device before any stream capture.
 //
 // All calls on a device share the one array and it keeps the last call's contents.
 // Nothing in it has to start at zero: every scratch element a kernel reads is written
 // earlier in the same call, and the first kernel resets the status word.  Calls that
 // overlap on the GPU (different streams, or different host threads without ordering)
-// race on the array; callers must order them.
+// race on the array; callers must order them.  The kernels report a bad page id, a bad
+// expert id or a device wait that ran out in the array's status word, which
+// smb_moe_noalloc_read_status returns.
 #include <mutex>
 
 #include "../../include/ae_b200.h"
@@ -34,26 +36,31 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 constexpr int kMaxScratchDevices = 64;
 
+// Device address of g_scratch per device, filled by the first successful lookup on that
+// device.  A failed lookup (for instance a first call made during a stream capture, or a
+// transient error) is not kept: the next call on that device tries again.
 struct ScratchSlot {
-  std::once_flag once;
+  std::mutex mu;
   void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
 };
 
 ScratchSlot g_scratch_slots[kMaxScratchDevices];
 
-// Device address of g_scratch on the current device (set up once per device).
+// Device address of g_scratch on the current device.
 int scratch_address(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return SMB_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxScratchDevices) return SMB_ERR_CUDA;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return smb::record_cuda_error(err);
+  if (dev < 0 || dev >= kMaxScratchDevices) return smb::record_cuda_error(cudaErrorInvalidDevice);
   ScratchSlot& s = g_scratch_slots[dev];
-  std::call_once(s.once, [&s] {
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.ptr == nullptr) {
     void* p = nullptr;
-    s.err = cudaGetSymbolAddress(&p, g_scratch);
-    s.ptr = (s.err == cudaSuccess) ? p : nullptr;
-  });
-  if (s.err != cudaSuccess || s.ptr == nullptr) return SMB_ERR_CUDA;
+    err = cudaGetSymbolAddress(&p, g_scratch);
+    if (err != cudaSuccess) return smb::record_cuda_error(err);
+    if (p == nullptr) return smb::record_cuda_error(cudaErrorInvalidSymbol);
+    s.ptr = p;
+  }
   *out = s.ptr;
   return SMB_OK;
 }
@@ -76,4 +83,15 @@ extern "C" int smb_moe_forward_noalloc(const void* x, const void* router_logits,
   if (rc != SMB_OK) return rc;
   return smb_moe_forward(x, router_logits, logits_dtype, pool, num_pages, page_of_expert, dtype, T, E, k, H, I,
                          renormalize, out, topk_weights, topk_ids, ws, kScratchBytes, stream);
+}
+
+// The status word the kernels of the last smb_moe_forward_noalloc call on the current
+// device wrote (it sits at offset 0 of the scratch, as in every workspace).  A call that
+// returned 0 has only been queued: a page id outside [0, num_pages), a given expert id
+// out of range or a device wait that ran out shows here, not in the return code.
+extern "C" int smb_moe_noalloc_read_status(smb_stream_t stream) {
+  void* ws = nullptr;
+  const int rc = scratch_address(&ws);
+  if (rc != SMB_OK) return rc;
+  return smb::read_status_word(static_cast<const int*>(ws), reinterpret_cast<cudaStream_t>(stream));
 }

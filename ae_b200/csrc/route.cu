@@ -198,8 +198,13 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     if (tid == 0) {
       s_ready = 1;
       if (a.link.p2p) {
+        const uint64_t tw = global_timer_ns();
         s_ready = wait_flags_sys(a.link.wait_flags, a.link.nranks, a.link.ctrl[0] + 1) ? 1 : 0;
         if (!s_ready) record_status(a.status, kDevTimeout);
+        if (cta == 0 && a.status != nullptr) {
+          DevTimers* tm = timers_of(a.status);
+          add_wait_time(&tm->recv_wait_ns, &tm->recv_waits, tw);
+        }
       }
     }
     __syncthreads();

@@ -36,6 +36,10 @@ import torch
 import torch.distributed as dist
 
 
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
 class CudaBackend:
     """The three compute steps on the sm_100a library (``smb_moe_ep_dispatch``,
     ``smb_moe_ep_experts``, ``smb_moe_ep_combine`` in ``include/ae_b200.h``).  Buffers and
@@ -65,8 +69,9 @@ class CudaBackend:
     def _stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def dispatch(self, x: torch.Tensor, logits: torch.Tensor, G: int, C: int):
-        """Route the local tokens and gather them into the exchange layout [G*(C+1), H]."""
+    def dispatch(self, x: torch.Tensor, logits: torch.Tensor, G: int, C: int, topk_weights=None, topk_ids=None):
+        """Route the local tokens and gather them into the exchange layout [G*(C+1), H];
+        optional routing outputs topk_weights fp32 / topk_ids int32 [T, k]."""
         from . import _native, ops
         T = x.shape[0]
         nbytes = ops.workspace_bytes(T, self.E, self.k, self.H, self.I, self.dtype)
@@ -74,7 +79,7 @@ class CudaBackend:
         send = self._buf(("send", G, C), shape=(G * (C + 1), self.H), dtype=self.dtype)
         _native.call("smb_moe_ep_dispatch", logits.data_ptr(), ops.logits_code(logits.dtype), x.data_ptr(),
                      self.code, T, self.E, self.k, self.H, self.I, int(self.renormalize), G, C, send.data_ptr(),
-                     None, None, ws.data_ptr(), ws.numel(), self._stream())
+                     _ptr(topk_weights), _ptr(topk_ids), ws.data_ptr(), ws.numel(), self._stream())
         return send, (ws, T)
 
     def experts(self, recv: torch.Tensor, G: int, C: int, pool: torch.Tensor, pages: torch.Tensor,
@@ -108,6 +113,8 @@ class PeerTransport:
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.C, self.H, self.code = C, H, ops.storage_code(dtype)
+        self.device = torch.device(device)
         lib = _native.load()
         nbytes = int(lib.smb_ep_arena_bytes(self.G, C, H, ops.storage_code(dtype)))
         if nbytes == 0:
@@ -134,6 +141,23 @@ class PeerTransport:
         self.arenas_ptr = ctypes.cast(self.arenas, ctypes.c_void_p)
         dist.barrier(group)
 
+    def resync(self):
+        """Bring every rank's exchange state back to epoch 0 (collective, between calls).
+
+        After a call in which a wait ran out (a rank that skipped the call, or one that was
+        late by more than the wait budget) the ranks' epochs disagree and every later call
+        would time out too.  Each rank finishes its queued work, the ranks meet, each zeroes
+        its own arena's control block and flags (``smb_ep_arena_reset``), and they meet
+        again, so that no rank's next dispatch can reach a peer before that peer's reset."""
+        from . import _native
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        with torch.cuda.device(self.device):
+            _native.call("smb_ep_arena_reset", ctypes.c_void_p(self.own), self.G, self.C, self.H, self.code,
+                         torch.cuda.current_stream(self.device).cuda_stream)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+
     def close(self):
         """Unmap the peers' arenas and free this rank's (collective)."""
         from . import _native
@@ -157,7 +181,7 @@ class P2PBackend(CudaBackend):
         super().__init__(E, k, H, I, dtype, device, renormalize)
         self.t = transport
 
-    def layer(self, x, logits, G, C, pool, pages, num_local):
+    def layer(self, x, logits, G, C, pool, pages, num_local, topk_weights=None, topk_ids=None):
         from . import _native, ops
         T = x.shape[0]
         nb = ops.workspace_bytes(max(T, 1), self.E, self.k, self.H, self.I, self.dtype)
@@ -169,7 +193,8 @@ class P2PBackend(CudaBackend):
         a = self.t.arenas_ptr
         _native.call("smb_moe_ep_dispatch_p2p", logits.data_ptr() if T else None, ops.logits_code(logits.dtype),
                      x.data_ptr() if T else None, self.code, T, self.E, self.k, self.H, self.I,
-                     int(self.renormalize), G, self.t.rank, C, a, None, None, ws.data_ptr(), ws.numel(), st)
+                     int(self.renormalize), G, self.t.rank, C, a, _ptr(topk_weights), _ptr(topk_ids), ws.data_ptr(),
+                     ws.numel(), st)
         _native.call("smb_moe_ep_experts_p2p", G, self.t.rank, C, a, pool.data_ptr(), pool.shape[0],
                      pages.data_ptr(), self.code, num_local, self.H, self.I, wse.data_ptr(), wse.numel(), st)
         _native.call("smb_moe_ep_combine_p2p", out.data_ptr() if T else None, self.code, T, self.E, self.k,
@@ -221,17 +246,24 @@ class ExpertParallelMoE:
         self.backend = backend or CudaBackend(num_experts, top_k, hidden_size, intermediate_size, pool.dtype,
                                               pool.device, renormalize)
 
-    def forward(self, x: torch.Tensor, router_logits: torch.Tensor, events=None) -> torch.Tensor:
-        """``events``: optional pair of CUDA events recorded around the local expert FFN."""
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor, events=None, topk_weights=None,
+                topk_ids=None) -> torch.Tensor:
+        """``events``: optional pair of CUDA events recorded around the local expert FFN
+        (NCCL transport); ``topk_weights`` fp32 / ``topk_ids`` int32 [T, k]: optional outputs
+        of the local tokens' routing."""
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of this layer")
         G, C = self.G, self.C
         if self.transport is not None:
-            return self.backend.layer(x, router_logits, G, C, self.pool, self.pages, self.E_loc)
+            return self.backend.layer(x, router_logits, G, C, self.pool, self.pages, self.E_loc, topk_weights,
+                                      topk_ids)
         # routing + gather into [G][1 header + C payload rows][H]; the headers carry the
         # per-expert counts, so one all-to-all moves counts and rows together
-        send, state = self.backend.dispatch(x, router_logits, G, C)
+        if topk_weights is None and topk_ids is None:
+            send, state = self.backend.dispatch(x, router_logits, G, C)
+        else:
+            send, state = self.backend.dispatch(x, router_logits, G, C, topk_weights=topk_weights, topk_ids=topk_ids)
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send, group=self.group)
         if events is not None:
@@ -244,6 +276,47 @@ class ExpertParallelMoE:
         return self.backend.combine(back, state, T, G, C)
 
     __call__ = forward
+
+    def timers(self, reset: bool = False) -> dict:
+        """This rank's device-side timers (``smb_moe_read_timers``) over the calls so far:
+        the local FFN kernel launches and, over peer memory, the time the receive router
+        waited for the sources' rows and the final combine for the returned rows."""
+        from . import ops
+        out = {}
+        for key, buf in self.backend._bufs.items():
+            if key[0] in ("ws_exp", "ws_src"):
+                t = ops.read_timers(buf, reset)
+                for name, v in t.items():
+                    out[name] = out.get(name, 0) + v
+        return out
+
+    def status(self) -> int:
+        """Device status of this rank's last call (0, or a negative SMB_ERR_* code such as
+        SMB_ERR_DEVICE_TIMEOUT when a wait for a peer ran out); synchronises."""
+        from . import _native
+        lib = _native.load()
+        worst = 0
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        for key, buf in self.backend._bufs.items():
+            if key[0] == "ws_src":
+                T = key[1]
+                rc = lib.smb_moe_read_status(buf.data_ptr(), buf.numel(), T, self.E, self.k, self.H, self.I,
+                                             self.backend.code, st)
+            elif key[0] == "ws_exp":
+                rc = lib.smb_moe_read_status(buf.data_ptr(), buf.numel(), key[1] * key[2], self.E_loc, 1, self.H,
+                                             self.I, self.backend.code, st)
+            else:
+                continue
+            if rc != 0 and worst == 0:
+                worst = int(rc)
+        return worst
+
+    def resync(self):
+        """Reset the peer-memory exchange of every rank to a common state after a failed
+        call (collective; see ``PeerTransport.resync``).  No-op for the NCCL transport,
+        whose collectives carry no state between calls."""
+        if self.transport is not None:
+            self.transport.resync()
 
     def close(self):
         """Release the exchange arenas of the p2p transport (collective)."""

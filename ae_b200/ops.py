@@ -69,6 +69,17 @@ class Workspace:
             return buf
 
     @classmethod
+    def lookup(cls, device: torch.device, stream=None) -> torch.Tensor | None:
+        """The buffer that calls on ``stream`` (default: the current stream) of ``device``
+        use, or None before the first call there."""
+        device = torch.device(device)
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        s = stream if stream is not None else torch.cuda.current_stream(device)
+        with cls._lock:
+            return cls._bufs.get((device.index, s.cuda_stream))
+
+    @classmethod
     def clear(cls):
         with cls._lock:
             cls._bufs.clear()
@@ -94,6 +105,10 @@ def splits(E: int, H: int, I: int, Tk: int) -> int:
     return _native.call("smb_moe_splits", E, H, I, Tk)
 
 
+def gate_up_slices(E: int, H: int, I: int, Tk: int) -> int:
+    return _native.call("smb_moe_gate_up_slices", E, H, I, Tk)
+
+
 def pool_geometry(pool: torch.Tensor, H: int):
     """(num_pages, I) of a page pool [P, 3*I*H]."""
     if pool.dim() != 2:
@@ -102,6 +117,18 @@ def pool_geometry(pool: torch.Tensor, H: int):
     if page % (3 * H):
         raise ValueError(f"page size {page} is not 3*I*H for H={H}")
     return P, page // (3 * H)
+
+
+def read_timers(ws: torch.Tensor, reset: bool = False) -> dict:
+    """Device-side kernel timers accumulated in workspace ``ws`` (``smb_moe_read_timers``):
+    ``ffn_ns`` / ``ffn_launches`` (FFN kernel launches, first CTA past its wait on the
+    router to the last CTA done) and the flag-wait times of the expert-parallel exchange.
+    Synchronises the current stream; ``reset`` then zeroes them, stream-ordered."""
+    import ctypes
+    t = _native.Timers()
+    _native.call("smb_moe_read_timers", ws.data_ptr(), ws.numel(), int(bool(reset)), ctypes.byref(t),
+                 _stream_ptr(ws.device))
+    return t.as_dict()
 
 
 def _status(ws: torch.Tensor, T, E, k, H, I, code, stream) -> int:
@@ -366,13 +393,17 @@ class StagedLayer:
 
         rows = up_to(Tk, 64) + 64
         S = splits(E, H, I, Tk)
+        K1 = gate_up_slices(E, H, I, Tk)
+        ntc = -(-Tk // 256) if Tk > 256 else 1
+        m1 = -(-I // 128)
+        ndone = 2 + E * S * ntc + (E * m1 * ntc if K1 > 1 else 0)
         o = 0
         off = {}
         # mirrors ae_b200/csrc/layout.h::make_ws_layout (checked against its total below)
-        for name, nb in (("status", 4 * 64), ("expert_off", 4 * (E + 1)), ("done", 4 * (E * S + 2)),
+        for name, nb in (("status", 4 * 64), ("expert_off", 4 * (E + 1)), ("done", 4 * ndone),
                          ("perm", 4 * Tk), ("inv", 4 * Tk), ("w", 4 * Tk), ("ids", 4 * Tk),
                          ("logits", 4 * self.T * E), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
-                         ("part", 4 * S * Tk * H)):
+                         ("part", 4 * S * Tk * H), ("gu", 4 * (K1 - 1) * rows * 2 * I)):
             off[name] = (o, nb)
             o = up(o + nb)
         if o != self.nbytes:
@@ -386,7 +417,7 @@ class StagedLayer:
         return {
             "expert_off": view("expert_off", torch.int32, (E + 1,)),
             "status": view("status", torch.int32, (64,)),
-            "done": view("done", torch.int32, (E * S + 2,)),
+            "done": view("done", torch.int32, (ndone,)),
             "perm": view("perm", torch.int32, (Tk,)),
             "inv": view("inv", torch.int32, (Tk,)),
             "w": view("w", torch.float32, (Tk,)),

@@ -7,18 +7,23 @@ A step is one pass of the MoE layer (route, expert FFN = gate/up GEMM + SiLU*mul
 GEMM, combine) over one verify batch of T synthetic tokens, inputs resident in HBM.  The
 timed region is K back-to-back replays of a CUDA graph holding one layer call, between
 CUDA events on the launching stream, bracketed by a barrier and a device synchronise,
-max over ranks (the eager, ctypes-per-call time is reported beside it).  Expert weights (2.8 GB for
-Mixtral-8x7B) are far larger than the 126 MB L2, so consecutive steps do not reuse
-weights from L2.
+max over ranks, after a soak of the same replays (the eager, ctypes-per-call time is
+reported beside it).  Expert weights (2.8 GB for Mixtral-8x7B) are far larger than the
+126 MB L2, so consecutive steps do not reuse weights from L2.  The FFN kernel's duration
+for the roofline comes from the library's device-side timers over exactly the K timed
+launches; the timed output is checked against the fp32 CPU oracle (``parity``).
 
 N > 1: expert parallelism (ae_b200/ep.py), strong scaling: the same verify batch of T
-tokens per step, T/N on each rank; rank r holds experts [r*E/N, (r+1)*E/N); rows are
-dispatched and returned with NCCL all-to-all.
+tokens per step, T/N on each rank; rank r holds experts [r*E/N, (r+1)*E/N); the kernels
+move the rows over NVLink peer memory (``--ep-transport p2p``, the default; NCCL
+all-to-alls are timed beside it), the whole batch's output is checked against the
+oracle on rank 0, and Mixtral-8x22B (C5) runs the same way.
 
-Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound), cpu_baseline (the CPU
-oracle port of the reference's arithmetic on this host), e2e (FusedMoE.forward with host
-inputs copied in and the output copied out every step), clocks, gpu_launches, kernels
-(per-kernel µs from a staged pass), sweep (other verify batch sizes).
+Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound), parity,
+cpu_baseline (the CPU oracle port of the reference's arithmetic on this host), e2e
+(FusedMoE.forward with host inputs copied in and the output copied out every step),
+clocks, gpu_launches, kernels_us (per-kernel µs from a staged pass), sweep (other verify
+batch sizes), c1_flushed (C1 with the L2 flushed), c5_single_gpu, and further blocks.
 
 ``--impl reference``: rank 0 times the reference's arithmetic on the host cores (the
 reference has no CPU expert path of its own; its Triton GPU kernel is the GPU side), the
@@ -159,7 +164,20 @@ def cpu_port_time(cfg, seed: int, max_seconds: float = 20.0, max_reps: int = 5, 
     return cfg.T / med, med, threads, len(times)
 
 
-def run_reference_arm(args, cfg, rank):
+def config_of(cfg, world: int) -> dict:
+    """The ``config`` object of the JSON line, the same on both arms for a given N."""
+    if world == 1:
+        return {"workload": cfg.name, "T": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
+                "parallelism": "single",
+                "l2": "inputs larger than L2 (expert weights %.2f GB per step)" % (cfg.weight_bytes() / 1e9)}
+    E_loc, T_r = cfg.E // world, cfg.T // world
+    return {"workload": cfg.name + f", expert-parallel over {world} GPUs ({T_r} tokens and {E_loc} experts per GPU)",
+            "T": cfg.T, "T_per_gpu": T_r, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
+            "experts_per_gpu": E_loc, "parallelism": f"ep{world}",
+            "l2": "inputs larger than L2 (expert weights %.2f GB per GPU per step)" % (cfg.weight_bytes(E_loc) / 1e9)}
+
+
+def run_reference_arm(args, cfg, rank, world):
     if rank != 0:
         return
     from ae_b200 import configs
@@ -196,7 +214,7 @@ def run_reference_arm(args, cfg, rank):
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": cfg.name, "T": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k},
+        "config": config_of(cfg, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU expert path (FusedMoE.forward_cpu is unreachable); this arm runs the "
@@ -207,20 +225,30 @@ def run_reference_arm(args, cfg, rank):
 
 # ---------------------------------------------------------------------------- GPU arm
 
-def algorithmic(cfg, touched: int, Tk: int, splits: int):
-    """Algorithmic bytes of the FFN kernel (touched experts' weights + its token rows in +
-    fp32 partials out) and of the whole layer (weights + tokens in and out + logits), and
-    the layer's flops."""
-    H, I, T, E = cfg.H, cfg.I, cfg.T, cfg.E
-    ffn = touched * 3 * H * I * 2 + Tk * H * 2 + splits * Tk * H * 4
+def algorithmic(cfg, touched: int, T: int | None = None):
+    """Algorithmic bytes (the survey's measurement rules: touched experts' weights, tokens
+    in and out, router logits; intermediate caches not counted) of the FFN kernel
+    (touched weights + the token rows it reads) and of the whole layer, and the layer's
+    flops."""
+    H, I, E = cfg.H, cfg.I, cfg.E
+    T = cfg.T if T is None else T
+    ffn = touched * 3 * H * I * 2 + T * H * 2
     layer = touched * 3 * H * I * 2 + 2 * T * H * 2 + T * E * 2
-    flops = 6 * H * I * Tk
+    flops = 6 * H * I * T * cfg.k
     return ffn, layer, flops
 
 
-def graph_of(fn, dev):
-    """Capture one call of ``fn`` into a CUDA graph (after a warm call on the capture
-    stream, so its workspace exists before capture)."""
+def touched_experts(logits, k: int, renormalize: bool = True) -> int:
+    """Experts that at least one token picks, from the library's own routing of the logits."""
+    from ae_b200 import ops
+    _, ids = ops.topk(logits, k, renormalize)
+    return int((torch.bincount(ids.flatten().long(), minlength=logits.shape[1]) > 0).sum())
+
+
+def graph_of(fn, dev, with_stream: bool = False):
+    """Capture one call of ``fn`` into a CUDA graph.  The warm call runs on the stream the
+    capture then uses, so the library's per-stream workspace exists before the capture and
+    the graph holds the kernels only (no allocation, no workspace initialisation)."""
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
@@ -228,10 +256,10 @@ def graph_of(fn, dev):
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, stream=side):
         fn()
     torch.cuda.synchronize(dev)
-    return g
+    return (g, side) if with_stream else g
 
 
 def timed_steps(fn, steps, stream):
@@ -253,8 +281,28 @@ def load_traffic(cfg_key):
         return None
 
 
+def parity_vs_oracle(out, x, logits, pool_cpu, pages, k, renormalize, ids=None, ref=None):
+    """Parity of a layer output against the fp32 CPU oracle on the same inputs: routing ids
+    bit-exact, max-abs and relative-L2 error, and the bar (max-abs <= 2e-2, or the
+    reference arithmetic's own error where that is larger; relative-L2 <= 1e-2)."""
+    from oracle import moe_oracle as mo  # the checker only
+    xc, lc = x.cpu(), logits.cpu()
+    rw, rids = mo.select_experts(lc, k, renormalize)
+    pc = pages.cpu()
+    ref = mo.stack_fused_moe(xc, pool_cpu, pc, rw, rids, rounding="fp32")
+    ref_r = mo.stack_fused_moe(xc, pool_cpu, pc, rw, rids, rounding="reference").float()
+    max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+    ref_err = float((ref_r - ref).abs().max())
+    bar = max(2e-2, ref_err)
+    res = {"max_abs": max_abs, "rel_l2": rel, "reference_rounding_max_abs": ref_err,
+           "bar": {"max_abs": bar, "rel_l2": 1e-2}, "within_bar": bool(max_abs <= bar and rel <= 1e-2),
+           "against": "fp32 CPU oracle (oracle/moe_oracle.py) on the timed inputs"}
+    if ids is not None:
+        res["ids_exact"] = bool((ids.cpu().numpy() == rids).all())
+    return res
+
+
 def run_ours(args, cfg, rank, world, dev):
-    import torch.distributed as dist
     from ae_b200 import configs, ops
     from ae_b200.layers.FusedMoE import FusedMoE
 
@@ -269,46 +317,45 @@ def run_ours(args, cfg, rank, world, dev):
     def step():
         ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out)
 
-    # warm-up and clock soak
     sampler = ClockSampler(device_uuid(dev))
     sampler.start()
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize(dev)
+    # eager launches (a host-side ctypes call per layer), for reference
+    eager = timed_steps(step, args.steps, stream)
+    # the timed region replays a CUDA graph of one layer call per step (the reference
+    # engine captures its verify step as well); launches are the same three kernels
+    graph, cap_stream = graph_of(step, dev, with_stream=True)
+    ws = ops.Workspace.lookup(dev, cap_stream)
+    # soak with the replays that are then timed, so the timed region starts in the power
+    # and clock state it runs in
     t_soak = time.time()
     soak_end = t_soak + args.soak
-    while time.time() < soak_end:
+    while True:
         for _ in range(20):
-            step()
+            graph.replay()
         torch.cuda.synchronize(dev)
-
-    # eager launches (host-side ctypes call per layer), for reference
-    torch.cuda.synchronize(dev)
-    eager = timed_steps(step, args.steps, stream)
-    # the timed region replays a CUDA graph of one layer call per step (the verify step
-    # of the reference engine is graph-captured as well); launches are the same kernels
-    graph = graph_of(step, dev)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+        if time.time() >= soak_end:
+            break
+    ops.read_timers(ws, reset=True)
     torch.cuda.synchronize(dev)
     elapsed = timed_steps(graph.replay, args.steps, stream)
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
     t_timed_end = time.time()
-    el = torch.tensor([elapsed], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(el, op=dist.ReduceOp.MAX)
-    elapsed = float(el.item())
+    # device-side timer of the FFN kernel over exactly the timed launches
+    tm = ops.read_timers(ws)
     clocks = sampler.summary(t_soak, t_timed_end)
     sampler.stop()
+    if tm["ffn_launches"] != args.steps:
+        raise RuntimeError(f"FFN timer saw {tm['ffn_launches']} launches in {args.steps} timed steps")
+    ffn_s = tm["ffn_ns"] / tm["ffn_launches"] * 1e-9
     if not torch.isfinite(out.float()).all():
         raise RuntimeError("non-finite layer output")
+    timed_out = out.clone()
 
-    # staged pass: per-kernel durations (events between the three launches of a layer call)
+    # staged pass: per-kernel durations from CUDA events between the three launches of a
+    # layer call (eager; a cross-check of the in-graph FFN timer)
     L = ops.StagedLayer(cfg.T, cfg.E, cfg.k, cfg.H, cfg.I, x.dtype, dev)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.staged_steps)]
     for i in range(3):
@@ -330,7 +377,8 @@ def run_ours(args, cfg, rank, world, dev):
     off = v["expert_off"].cpu()
     touched = int(((off[1:] - off[:-1]) > 0).sum())
     splits = ops.splits(cfg.E, cfg.H, cfg.I, Tk)
-    ffn_bytes, layer_bytes, flops = algorithmic(cfg, touched, Tk, splits)
+    ffn_bytes, layer_bytes, flops = algorithmic(cfg, touched)
+    del L
 
     # end to end through the drop-in module: host inputs in, host output out, every step
     moe = FusedMoE(cfg.E, cfg.k, cfg.H, cfg.I, params_dtype=x.dtype, renormalize=cfg.renormalize, tp_size=1)
@@ -350,17 +398,24 @@ def run_ours(args, cfg, rank, world, dev):
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
     e2e_el = timed_steps(e2e_step, args.steps, stream)
-    t = torch.tensor([e2e_el], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_el = float(t.item())
 
-    # other verify batch sizes of the same layer (rank 0 view, N=1 only)
+    # parity of the timed output against the fp32 oracle (rank 0, N = 1), and the routing
+    # ids of one more call on the same inputs (whose output must equal the timed one)
+    parity = None
+    pool_cpu = None
+    if rank == 0 and not args.no_parity:
+        pool_cpu = pool.cpu()
+        w_chk = torch.empty(cfg.T, cfg.k, dtype=torch.float32, device=dev)
+        ids_chk = torch.empty(cfg.T, cfg.k, dtype=torch.int32, device=dev)
+        again = ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, topk_weights=w_chk, topk_ids=ids_chk)
+        torch.cuda.synchronize(dev)
+        parity = parity_vs_oracle(timed_out, x, logits, pool_cpu, pages, cfg.k, cfg.renormalize, ids=ids_chk)
+        parity["repeat_bitwise_equal"] = bool(torch.equal(again, timed_out))
+
+    # other verify batch sizes of the same layer (N = 1)
     sweep = {}
-    if world == 1 and not args.no_sweep:
+    if not args.no_sweep:
         for Ts in args.sweep:
             if Ts == cfg.T:
                 continue
@@ -379,16 +434,17 @@ def run_ours(args, cfg, rank, world, dev):
             n = max(10, args.steps // 2)
             el_s = timed_steps(gs.replay, n, stream)
             us = el_s / n * 1e6
+            t_s = touched_experts(ls, cfg.k, cfg.renormalize)
             sweep[f"T{Ts}"] = {"us_per_layer": round(us, 2), "tokens_per_s": round(Ts / (el_s / n), 1),
-                               "layer_hbm_frac": round(algorithmic(
-                                   configs.MoEConfig(cfg.name, cfg.H, cfg.I, cfg.E, cfg.k, Ts, cfg.router_std),
-                                   cfg.E, Ts * cfg.k, splits)[1] / (el_s / n) / 1e9 / hbm_peak, 4)}
+                               "experts_touched": t_s,
+                               "layer_hbm_frac": round(algorithmic(cfg, t_s, Ts)[1] / (el_s / n) / 1e9 / hbm_peak, 4)}
+            del gs
 
     # the whole MixtralMoE block (gate + experts): gate fused into the routing launch vs.
     # the reference's arrangement of a separate half-precision gate GEMM (cuBLAS, like
     # ReplicatedLinear) followed by the layer
     gated = None
-    if world == 1 and not args.no_sweep:
+    if not args.no_sweep:
         xg, wg = configs.make_gate_inputs(cfg, dev, seed=2)
         og = torch.empty_like(xg)
 
@@ -413,42 +469,52 @@ def run_ours(args, cfg, rank, world, dev):
                 for _ in range(3):
                     gg.replay()
                 samples[name].append(timed_steps(gg.replay, n, stream) / n * 1e6)
-        for name, v in samples.items():
-            gated[f"{name}_us_per_layer"] = round(statistics.median(v), 2)
+        for name, sv in samples.items():
+            gated[f"{name}_us_per_layer"] = round(statistics.median(sv), 2)
         del graphs
+
+    # the small configuration of the reference's CPU path (C1), L2 flushed between replays
+    c1 = None
+    if not args.no_sweep:
+        c1 = bench_flushed_config(configs.BY_KEY["c1"], dev, stream, max(20, args.steps), hbm_peak)
+
+    # Mixtral-8x22B (C5, T = 512) on this GPU: the expert-parallel configuration's N = 1 point
+    c5 = None
+    if not args.no_sweep:
+        c5 = bench_single_config(configs.BY_KEY["c5"], dev, stream, max(10, args.steps // 2), hbm_peak)
 
     # the fine-grained configuration with a shared expert (60 routed experts of I 1408,
     # top-4, shared expert I 5632 as 4 pseudo-experts in the same launch, Zipf routing)
     fine = None
-    if world == 1 and not args.no_sweep:
+    if not args.no_sweep:
         fine = bench_shared_config(configs.BY_KEY["c3"], dev, stream, max(10, args.steps // 2), hbm_peak)
 
     # the 32-layer verify step (Mixtral-8x7B architecture, batch 4 x 32-token draft tree on
     # a 2048-token KV cache), MoE layers isolated by CUDA events around each MoE call
     verify = None
-    if world == 1 and not args.no_sweep and not args.no_verify:
+    if not args.no_sweep and not args.no_verify:
         verify = bench_verify_step(dev, stream, hbm_peak)
 
     # expert pages streamed from page-locked host memory while the layer runs (all 8
     # experts cross PCIe, as with the reference's decode_weight_cache_ratio = 0)
     streamed = None
-    if world == 1 and not args.no_sweep:
+    if not args.no_sweep:
         streamed = bench_streaming(cfg, pool, pages, x, logits, dev, stream)
 
     # CPU baseline (rank 0, N = 1)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        pool_cpu = pool.cpu()
+    if rank == 0 and not args.no_cpu_baseline:
+        if pool_cpu is None:
+            pool_cpu = pool.cpu()
         tps, sec, threads, reps = cpu_port_time(cfg, 0, pool_cpu=pool_cpu, x=x.cpu(), logits=logits.cpu())
         cpu = {"value": round(tps, 2), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{reps} full layer calls of {cfg.T} tokens ({cfg.name}), median {sec * 1000:.1f} ms, "
                          f"oracle CPU restatement, bf16 storage / fp32 accumulate, {threads} threads"}
-        del pool_cpu
+    del pool_cpu
 
     if rank != 0:
         return
     step_s = elapsed / args.steps
-    ffn_s = kern_us["ffn"] * 1e-6
     achieved = ffn_bytes / ffn_s / 1e9
     traffic = load_traffic(args.config)
     line = {
@@ -468,19 +534,25 @@ def run_ours(args, cfg, rank, world, dev):
         "dtype": "bf16",
         "data": "synthetic: expert weights N(0,0.02) bf16, tokens N(0,1), router logits x@Wr^T "
                 f"(Wr std {cfg.router_std:.4g})",
-        "config": {"workload": cfg.name, "T": cfg.T, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
-                   "experts_touched": touched, "splits": splits,
-                   "parallelism": "replicas" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (expert weights %.2f GB per step)" % (cfg.weight_bytes() / 1e9)},
+        "config": config_of(cfg, world),
+        "layout": {"experts_touched": touched, "splits": splits},
         "roofline": {"bound": "hbm", "kernel": "ffn_gemm_kernel (gate/up + down, one launch)",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                     "alg_bytes_per_launch": ffn_bytes, "traffic": traffic},
+                     "alg_bytes_per_launch": ffn_bytes,
+                     "duration_us": round(ffn_s * 1e6, 2),
+                     "timing": f"device timer of every FFN launch in the timed region ({tm['ffn_launches']} "
+                               "launches: first CTA past its wait on the router to the last CTA done, "
+                               "%globaltimer), averaged",
+                     "traffic": traffic},
         "layer_roofline": {"alg_bytes": layer_bytes, "achieved_gbs": round(layer_bytes / step_s / 1e9, 1),
                            "frac_hbm": round(layer_bytes / step_s / 1e9 / hbm_peak, 4),
                            "tflops": round(flops / step_s / 1e12, 2),
                            "frac_tensor": round(flops / step_s / 1e12 / tc_peak, 4)},
         "kernels_us": {n: round(u, 2) for n, u in kern_us.items()},
+        "kernels_timing": "CUDA events between eager launches of the three kernels (staged pass after the timed "
+                          "region)",
+        "parity": parity,
         "cpu_baseline": cpu,
         "e2e": {"value": round(world * cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size() + logits.numel() * logits.element_size(),
@@ -489,12 +561,87 @@ def run_ours(args, cfg, rank, world, dev):
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
         "sweep": sweep,
+        "c1_flushed": c1,
+        "c5_single_gpu": c5,
         "gated_block": gated,
         "shared_expert_config": fine,
         "verify_32_layers": verify,
         "streamed_pages": streamed,
     }
     emit(line)
+
+
+def bench_single_config(cfg, dev, stream, n, hbm_peak):
+    """Graph-replay time of one layer call of another routed configuration on this GPU
+    (inputs larger than L2), with its HBM roofline fraction and the FFN kernel's device timer."""
+    from ae_b200 import configs, ops
+    pool = configs.make_pool(cfg, dev, seed=0)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=0)
+    out = torch.empty_like(x)
+
+    def step():
+        ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out)
+
+    for _ in range(3):
+        step()
+    gr, cs = graph_of(step, dev, with_stream=True)
+    ws = ops.Workspace.lookup(dev, cs)
+    for _ in range(3):
+        gr.replay()
+    ops.read_timers(ws, reset=True)
+    el = timed_steps(gr.replay, n, stream)
+    tm = ops.read_timers(ws)
+    touched = touched_experts(logits, cfg.k, cfg.renormalize)
+    ffn_b, layer_b, flops = algorithmic(cfg, touched)
+    t = el / n
+    ffn_s = tm["ffn_ns"] / max(1, tm["ffn_launches"]) * 1e-9
+    del gr, pool
+    torch.cuda.empty_cache()
+    return {"workload": cfg.name, "T": cfg.T, "us_per_layer": round(t * 1e6, 2),
+            "tokens_per_s": round(cfg.T / t, 1), "experts_touched": touched, "alg_bytes": layer_b,
+            "layer_hbm_frac": round(layer_b / t / 1e9 / hbm_peak, 4),
+            "ffn_us": round(ffn_s * 1e6, 2), "ffn_hbm_frac": round(ffn_b / ffn_s / 1e9 / hbm_peak, 4),
+            "splits": ops.splits(cfg.E, cfg.H, cfg.I, cfg.T * cfg.k),
+            "api": "ae_b200.ops.moe_forward (smb_moe_forward)", "timing": f"{n} graph replays"}
+
+
+def bench_flushed_config(cfg, dev, stream, n, hbm_peak, flush_bytes: int = 256 << 20):
+    """Layer time of a configuration whose weights are only ~1.4x the L2 (C1: 176 MB): each
+    replay is timed alone between CUDA events, with a 256 MB buffer written before it
+    (outside the events) so that no weights are served from L2."""
+    from ae_b200 import configs, ops
+    pool = configs.make_pool(cfg, dev, seed=0)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=0)
+    out = torch.empty_like(x)
+    scratch = torch.empty(flush_bytes, dtype=torch.uint8, device=dev)
+
+    def step():
+        ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out)
+
+    for _ in range(3):
+        step()
+    gr = graph_of(step, dev)
+    times = []
+    for i in range(n + 3):
+        scratch.fill_(i & 0xFF)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        gr.replay()
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b) * 1e-3)
+    touched = touched_experts(logits, cfg.k, cfg.renormalize)
+    _, layer_b, _ = algorithmic(cfg, touched)
+    t = statistics.median(times)
+    del gr, pool, scratch
+    return {"workload": cfg.name, "T": cfg.T, "us_per_layer": round(t * 1e6, 2),
+            "tokens_per_s": round(cfg.T / t, 1), "experts_touched": touched, "alg_bytes": layer_b,
+            "layer_hbm_frac": round(layer_b / t / 1e9 / hbm_peak, 4),
+            "l2": f"{flush_bytes >> 20} MB buffer written before every timed replay (outside the events)",
+            "timing": f"median of {n} single graph replays"}
 
 
 def bench_shared_config(cfg, dev, stream, n, hbm_peak):
@@ -529,8 +676,7 @@ def bench_shared_config(cfg, dev, stream, n, hbm_peak):
         gr.replay()
     torch.cuda.synchronize(dev)
     el = timed_steps(gr.replay, n, stream)
-    ids = torch.topk(logits.float(), cfg.k, dim=1).indices
-    touched = int((torch.bincount(ids.flatten(), minlength=cfg.E) > 0).sum())
+    touched = touched_experts(logits, cfg.k, cfg.renormalize)
     alg = (touched * 3 * cfg.I * H + 3 * Is * H) * 2 + 2 * cfg.T * H * 2 + cfg.T * cfg.E * 2
     us = el / n * 1e6
     del gr
@@ -634,13 +780,95 @@ def bench_verify_step(dev, stream, hbm_peak, steps: int = 5):
     return out
 
 
+def ep_time(moe, x, logits, dev, stream, steps, soak=0.0):
+    """Graph-replay time of ``steps`` expert-parallel layer calls (max over ranks) with the
+    ranks' device timers over exactly those calls.  Returns (seconds, timers per rank as a
+    [world, 6] tensor on every rank, launch mode)."""
+    import torch.distributed as dist
+
+    def step():
+        return moe(x, logits)
+
+    graph = None
+    mode = "cuda_graph (one expert-parallel layer call per replay)"
+    try:
+        graph = graph_of(step, dev)
+        run = graph.replay
+        for _ in range(3):
+            run()
+    except Exception as exc:  # capture unsupported here: time the eager calls instead
+        mode = f"eager (graph capture failed: {type(exc).__name__})"
+        run = step
+    torch.cuda.synchronize(dev)
+    end = time.time() + soak
+    while True:
+        for _ in range(20):
+            run()
+        torch.cuda.synchronize(dev)
+        if time.time() >= end:
+            break
+    moe.timers(reset=True)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    elapsed = timed_steps(run, steps, stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    tm = moe.timers()
+    mine = torch.tensor([elapsed, tm.get("ffn_ns", 0) / max(1, tm.get("ffn_launches", 0)) * 1e-3,
+                         tm.get("recv_wait_ns", 0) / max(1, tm.get("recv_waits", 0)) * 1e-3,
+                         tm.get("combine_wait_ns", 0) / max(1, tm.get("combine_waits", 0)) * 1e-3,
+                         tm.get("ffn_launches", 0), tm.get("recv_waits", 0)], device=dev, dtype=torch.float64)
+    every = [torch.empty_like(mine) for _ in range(dist.get_world_size())]
+    dist.all_gather(every, mine)
+    every = torch.stack(every)
+    del graph
+    torch.cuda.synchronize(dev)
+    return float(every[:, 0].max()), every.cpu(), mode
+
+
+def ep_parity(cfg, moe, x, logits, rank, world, dev):
+    """Every rank's output and routing ids of one more call on its timed inputs, gathered
+    on rank 0 and checked over the whole batch against the fp32 CPU oracle (all experts,
+    the same seeded pages) and against the single-GPU library layer.  Collective."""
+    import torch.distributed as dist
+    from ae_b200 import configs, ops
+    T_r = x.shape[0]
+    w = torch.empty(T_r, cfg.k, dtype=torch.float32, device=dev)
+    ids = torch.empty(T_r, cfg.k, dtype=torch.int32, device=dev)
+    out = moe(x, logits, topk_weights=w, topk_ids=ids).clone()
+    torch.cuda.synchronize(dev)
+    outs = [torch.empty_like(out) for _ in range(world)]
+    idss = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(outs, out)
+    dist.all_gather(idss, ids)
+    res = None
+    if rank == 0:
+        from oracle import moe_oracle as mo  # the checker only
+        xs, ls = zip(*[configs.make_inputs(cfg, dev, seed=r, T=T_r) for r in range(world)])
+        xs, ls = torch.cat(xs), torch.cat(ls)
+        full = configs.make_pool(cfg, dev, seed=0)
+        pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+        single = ops.moe_forward(xs, ls, full, pages, cfg.k, cfg.renormalize)
+        torch.cuda.synchronize(dev)
+        got = torch.cat(outs)
+        res = parity_vs_oracle(got, xs, ls, full.cpu(), pages, cfg.k, cfg.renormalize, ids=torch.cat(idss))
+        sm, sr = mo.error_metrics(got.float().cpu(), single.float().cpu())
+        res["vs_single_gpu_layer"] = {"max_abs": sm, "rel_l2": sr}
+        res["against"] += f"; whole batch of {cfg.T} tokens gathered from {world} ranks"
+        del full, single
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return res
+
+
 def run_ep(args, cfg, rank, world, dev):
     """N > 1: expert parallelism, strong scaling.  One verify batch of T tokens per step is
     spread over the N ranks (T/N each); rank r holds experts [r*E/N, (r+1)*E/N); rows are
     dispatched and returned by the kernels over peer memory (the default, ``--ep-transport
     p2p``) or with fixed-capacity NCCL all-to-alls (``nccl``), with no host synchronisation
     either way, so the step is replayed from a CUDA graph (ae_b200/ep.py).  The other
-    transport is timed on the same ranks for comparison."""
+    transport is timed on the same ranks for comparison, the output is checked against the
+    oracle, and Mixtral-8x22B (C5) is timed the same way."""
     import torch.distributed as dist
     from ae_b200 import configs
     from ae_b200.ep import ExpertParallelMoE
@@ -664,55 +892,25 @@ def run_ep(args, cfg, rank, world, dev):
         step()
     torch.cuda.synchronize(dev)
     eager = timed_steps(step, args.steps, stream)
-    mode = ("cuda_graph (one expert-parallel layer call per replay: rows moved by the kernels over peer "
-            "memory, no collective)" if args.ep_transport == "p2p" else
-            "cuda_graph (one expert-parallel layer call per replay, NCCL inside the graph)")
-    graph = None
-    try:
-        graph = graph_of(step, dev)
-        run = graph.replay
-        for _ in range(3):
-            run()
-    except Exception as exc:  # capture unsupported here: time the eager calls instead
-        mode = f"eager (graph capture failed: {type(exc).__name__})"
-        run = step
-    torch.cuda.synchronize(dev)
-    t_soak = time.time()
-    soak_end = t_soak + args.soak
-    while time.time() < soak_end:
-        for _ in range(20):
-            run()
-        torch.cuda.synchronize(dev)
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    elapsed = timed_steps(run, args.steps, stream)
-    torch.cuda.synchronize(dev)
-    dist.barrier()
-    t_end = time.time()
-    el = torch.tensor([elapsed, eager], device=dev, dtype=torch.float64)
+    el = torch.tensor([eager], device=dev, dtype=torch.float64)
     dist.all_reduce(el, op=dist.ReduceOp.MAX)
-    elapsed, eager = float(el[0].item()), float(el[1].item())
+    eager = float(el.item())
+    t_soak = time.time()
+    elapsed, per_rank, mode = ep_time(moe, x, logits, dev, stream, args.steps, soak=args.soak)
+    t_end = time.time()
     clocks = sampler.summary(t_soak, t_end)
     sampler.stop()
+    if args.ep_transport == "p2p":
+        mode = mode.replace("per replay)", "per replay: rows moved by the kernels over peer memory, no collective)")
+
+    parity = None if args.no_parity else ep_parity(cfg, moe, x, logits, rank, world, dev)
 
     # the same layer with the other transport, graph replays, max over ranks
     other = "nccl" if args.ep_transport == "p2p" else "p2p"
     moe2 = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r, transport=other)
-
-    def step2():
-        return moe2(x, logits)
-
     for _ in range(3):
-        step2()
-    g2 = graph_of(step2, dev)
-    for _ in range(3):
-        g2.replay()
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    t2 = torch.tensor([timed_steps(g2.replay, args.steps, stream) / args.steps], device=dev, dtype=torch.float64)
-    dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    del g2
-    torch.cuda.synchronize(dev)
+        moe2(x, logits)
+    t2, _, _ = ep_time(moe2, x, logits, dev, stream, args.steps)
     moe2.close()
 
     # the local expert FFN of a step on the rows this rank received, replayed from a
@@ -757,13 +955,21 @@ def run_ep(args, cfg, rank, world, dev):
     t = torch.tensor([e2e_el], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_el = float(t.item())
-    del graph
     torch.cuda.synchronize(dev)
     moe.close()
+    del pool
+
+    # Mixtral-8x22B (C5): T = 512 per step, T/N tokens and E/N experts per rank
+    c5 = None
+    if not args.no_sweep:
+        c5 = ep_config_block(configs.BY_KEY["c5"], rank, world, dev, stream, max(10, args.steps // 2),
+                             hbm_peak, args.ep_transport, args.no_parity)
+
     if rank != 0:
         return
     step_s = elapsed / args.steps
     achieved = float(ach.item())
+    pr = per_rank.numpy()
     line = {
         "metric": METRIC,
         "value": round(cfg.T * args.steps / elapsed, 2),
@@ -781,26 +987,57 @@ def run_ep(args, cfg, rank, world, dev):
         "dtype": "bf16",
         "data": "synthetic: expert weights N(0,0.02) bf16, tokens N(0,1), router logits x@Wr^T "
                 f"(Wr std {cfg.router_std:.4g})",
-        "config": {"workload": cfg.name + f", expert-parallel over {world} GPUs ({T_r} tokens and {E_loc} "
-                                          "experts per GPU)",
-                   "T": cfg.T, "T_per_gpu": T_r, "H": cfg.H, "I": cfg.I, "E": cfg.E, "k": cfg.k,
-                   "experts_per_gpu": E_loc, "parallelism": f"ep{world}",
-                   "l2": "inputs larger than L2 (expert weights %.2f GB per GPU per step)"
-                         % (cfg.weight_bytes(E_loc) / 1e9)},
+        "config": config_of(cfg, world),
         "roofline": {"bound": "hbm", "kernel": "local experts on the received rows (smb_moe_ep_experts: "
                                                 "route_kernel + ffn_gemm_kernel + combine_kernel), slowest rank",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None},
+        "per_rank_device_timers_us": {
+            "ffn": [round(float(v), 2) for v in pr[:, 1]],
+            "recv_flag_wait": [round(float(v), 2) for v in pr[:, 2]],
+            "return_flag_wait": [round(float(v), 2) for v in pr[:, 3]],
+            "timing": "device timers over the timed replays (means per call): FFN kernel (first CTA past its "
+                      "wait to last CTA done), expert-side wait for the sources' rows, source-side wait for "
+                      "the returned rows"},
+        "parity": parity,
         "cpu_baseline": None,
         "e2e": {"value": round(cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
                 "h2d_bytes_per_step": world * (x.numel() * x.element_size() + logits.numel() * logits.element_size()),
                 "d2h_bytes_per_step": world * x.numel() * x.element_size(),
                 "api": f"ae_b200.ep.ExpertParallelMoE.forward (transport={args.ep_transport})"},
-        f"{other}_transport_us_per_layer": round(float(t2.item()) * 1e6, 2),
-        "gpu_launches": 5 * args.steps,
+        f"{other}_transport_us_per_layer": round(t2 / args.steps * 1e6, 2),
+        "gpu_launches": (3 if args.ep_transport == "p2p" else 5) * args.steps,
         "clocks": clocks,
+        "c5_expert_parallel": c5,
     }
     emit(line)
+
+
+def ep_config_block(cfg, rank, world, dev, stream, n, hbm_peak, transport, no_parity):
+    """Another configuration through the expert-parallel layer on the same ranks: graph
+    replays, max over ranks, per-GPU HBM fraction, parity over the whole batch."""
+    from ae_b200 import configs
+    from ae_b200.ep import ExpertParallelMoE
+    E_loc, T_r = cfg.E // world, cfg.T // world
+    pool = configs.make_pool(cfg, dev, seed=0, experts=range(rank * E_loc, (rank + 1) * E_loc))
+    x, logits = configs.make_inputs(cfg, dev, seed=rank, T=T_r)
+    moe = ExpertParallelMoE(cfg.E, cfg.k, cfg.H, cfg.I, pool, max_tokens=T_r, transport=transport)
+    for _ in range(3):
+        moe(x, logits)
+    el, per_rank, _ = ep_time(moe, x, logits, dev, stream, n)
+    parity = None if no_parity else ep_parity(cfg, moe, x, logits, rank, world, dev)
+    moe.close()
+    del moe, pool
+    torch.cuda.empty_cache()
+    t = el / n
+    per_gpu_bytes = cfg.weight_bytes(E_loc)
+    pr = per_rank.numpy()
+    return {"workload": cfg.name + f", expert-parallel over {world} GPUs ({T_r} tokens and {E_loc} experts per GPU)",
+            "T": cfg.T, "us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(cfg.T / t, 1),
+            "per_gpu_weight_bytes": per_gpu_bytes,
+            "per_gpu_hbm_frac": round(per_gpu_bytes / t / 1e9 / hbm_peak, 4),
+            "ffn_us_per_rank": [round(float(v), 2) for v in pr[:, 1]],
+            "parity": parity, "transport": transport, "timing": f"{n} graph replays, max over ranks"}
 
 
 def run_ep_rank(args, cfg, dev):
@@ -879,6 +1116,7 @@ def main():
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-alls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -890,7 +1128,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        run_reference_arm(args, cfg, rank)
+        run_reference_arm(args, cfg, rank, world)
         return
 
     from ae_b200 import build

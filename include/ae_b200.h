@@ -13,8 +13,9 @@
  * The reference has no FFI for this path (it is Python + Triton); these entry points
  * are what a binding of that Python surface calls.  Conventions:
  *   - every pointer is a device pointer unless stated; the caller owns every buffer,
- *     including the workspace (size from smb_moe_workspace_bytes); nothing here
- *     allocates device memory;
+ *     including the workspace (size from smb_moe_workspace_bytes); no layer call
+ *     allocates device memory (the one allocating entry point is smb_ep_ipc_alloc, a
+ *     set-up call of the peer-memory exchange);
  *   - calls are asynchronous and ordered on `stream` (a cudaStream_t); distinct streams
  *     may call concurrently with distinct workspaces;
  *   - return 0 (SMB_OK) or a negative SMB_ERR_* code; nothing aborts the process;
@@ -80,6 +81,12 @@ SMB_API size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dt
 /* Split-K factor the down projection uses for these sizes (Tk = T*k) on the current
  * device. */
 SMB_API int smb_moe_splits(int E, int H, int I, int Tk);
+
+/* K slices the gate/up projection is cut into for these sizes on the current device (1, or
+ * 2 / 4 when the touched experts give fewer gate/up units than SMs, e.g. one expert per
+ * rank of an expert-parallel layer; the slices before the last store fp32 partials in the
+ * workspace that the last slice adds). */
+SMB_API int smb_moe_gate_up_slices(int E, int H, int I, int Tk);
 
 /* Router: softmax over E in fp32, top-k (ties to the lower expert index), optional
  * renormalisation; then the expert-major permutation (positions in the workspace).  Replaces select_experts (FusedMoE.py:174-185) + moe_align_block_size
@@ -185,6 +192,14 @@ SMB_API int smb_ep_ipc_alloc(size_t bytes, void** dev_ptr, void* ipc_handle /* 6
 SMB_API int smb_ep_ipc_open(const void* ipc_handle, void** peer_ptr);
 SMB_API int smb_ep_ipc_close(void* peer_ptr);
 SMB_API int smb_ep_ipc_free(void* dev_ptr);
+/* Zero this rank's arena control block and flags (epoch 0, tickets 0, no flag raised), on
+ * `stream`.  Recovery after a call in which some rank's wait ran out (SMB_ERR_DEVICE_TIMEOUT,
+ * e.g. a rank that skipped the call): the ranks' epochs no longer agree, so every rank
+ * finishes its queued work, the ranks meet (host barrier), each resets its own arena, and
+ * they meet again before the next call.  No kernel of the exchange may be running on any
+ * rank meanwhile.  The reference has no expert-parallel path; its transfer engine bounds
+ * its waits and reports failures the same way (specmoe/backend/htod_transfer_engine.py:347-370). */
+SMB_API int smb_ep_arena_reset(void* arena, int G, int C, int H, int dtype, smb_stream_t stream);
 SMB_API int smb_moe_ep_dispatch_p2p(const void* router_logits, int logits_dtype, const void* x, int dtype, int T,
                                     int E, int k, int H, int I, int renormalize, int G, int rank, int C,
                                     void* const* arenas, float* topk_weights, int32_t* topk_ids, void* ws,
@@ -280,6 +295,14 @@ SMB_API int smb_moe_forward_noalloc(const void* x, const void* router_logits, in
                                     int k, int H, int I, int renormalize, void* out, float* topk_weights,
                                     int32_t* topk_ids, smb_stream_t stream);
 
+/* Device status of the last smb_moe_forward_noalloc call on the current device, read
+ * synchronously on `stream` from the library's scratch (0, SMB_ERR_DEVICE_TIMEOUT,
+ * SMB_ERR_BAD_PAGE or SMB_ERR_BAD_EXPERT): the companion of smb_moe_read_status for
+ * callers that hold no workspace.  A noalloc call that returned 0 has only been queued;
+ * problems the kernels find (a page id outside [0, num_pages) is skipped, not faulted)
+ * show here.  No counterpart in the reference. */
+SMB_API int smb_moe_noalloc_read_status(smb_stream_t stream);
+
 /* Block-padded layout of moe_align_block_size (fused_moe_kernel.py:16-85):
  * sorted_ids [numel + E*(block_size-1)] (pad value numel), expert_ids
  * [cdiv(numel + E*(block_size-1), block_size)] (-1 past the last used block),
@@ -291,6 +314,28 @@ SMB_API int smb_moe_align_block_size(const int32_t* topk_ids, int numel, int E, 
  * (0, SMB_ERR_DEVICE_TIMEOUT, SMB_ERR_BAD_PAGE or SMB_ERR_BAD_EXPERT). */
 SMB_API int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype,
                         smb_stream_t stream);
+
+/* Device-side timers accumulated in a workspace's control block by the kernels that
+ * used it (nanoseconds of the GPU's global timer), for profiling without a profiler, in
+ * CUDA-graph replays too.  The reference has no counterpart (its Triton launches are
+ * timed from the host, specmoe/optimizer/performance_simulator/operators/gpu_fused_moe.py:84-116).
+ *   ffn_ns / ffn_launches: per FFN kernel launch, from the first CTA past its wait on the
+ *     router to the last CTA done, summed;
+ *   recv_wait_ns / recv_waits: expert side of the peer-memory exchange, time the receive
+ *     router waited for the sources' flags;
+ *   combine_wait_ns / combine_waits: source side, time the final combine waited for the
+ *     returned rows.
+ * Reads synchronously on `stream`; reset != 0 then zeroes the timers (stream-ordered). */
+typedef struct smb_timers {
+  uint64_t ffn_ns;
+  uint64_t recv_wait_ns;
+  uint64_t combine_wait_ns;
+  uint32_t ffn_launches;
+  uint32_t recv_waits;
+  uint32_t combine_waits;
+  uint32_t reserved;
+} smb_timers_t;
+SMB_API int smb_moe_read_timers(const void* ws, size_t ws_bytes, int reset, smb_timers_t* out, smb_stream_t stream);
 
 #ifdef __cplusplus
 }

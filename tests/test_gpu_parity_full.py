@@ -1,0 +1,122 @@
+"""Parity at the headline and full expert sizes, through the same call the bench times.
+
+The bench line's workload (Mixtral-8x7B, T = 256: split-K S = 2, 64-token tiles), a
+smaller verify batch of the same layer (T = 64) and Mixtral-8x22B at T = 512 (128+ tokens
+per expert: the TMA token-tile path) run through ``ops.moe_forward`` (``smb_moe_forward``)
+on the bench's own seeded inputs (``ae_b200.configs``) and are checked against the fp32
+CPU oracle (``oracle.stack_fused_moe``, restating
+specmoe/layers/fused_moe_kernel.py:253-349):
+
+* routing ids, weights and the expert-major permutation bit-exact (ids / permutation) and
+  to fp32 rounding (weights);
+* hidden states: relative-L2 <= 1e-2 and max-abs <= 2e-2, or, where larger, the error of
+  the reference's own arithmetic at these sizes (the oracle's reference-rounding mode,
+  which stores the SiLU*mul activations and each expert's weighted output in bf16 like the
+  reference's cache2 / cache3, against fp32).  Each case prints its measured errors next
+  to that bar (``PARITY`` lines, ``pytest -s``).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_L2 = 2e-2, 1e-2
+
+
+@pytest.mark.parametrize("key,T", [("c2-256", 256), ("c2-256", 64), ("c5", 512)])
+def test_headline_layer_vs_oracle(key, T):
+    from ae_b200 import configs, ops
+    cfg = configs.BY_KEY[key]
+    dev = torch.device("cuda", 0)
+    pool = configs.make_pool(cfg, dev, seed=0)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=0, T=T)
+    w = torch.empty(T, cfg.k, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, cfg.k, dtype=torch.int32, device=dev)
+    out = ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, topk_weights=w, topk_ids=ids)
+    # the permutation of the same routing, from the router alone
+    L = ops.StagedLayer(T, cfg.E, cfg.k, cfg.H, cfg.I, x.dtype, dev)
+    L.route(logits, x, cfg.renormalize)
+    torch.cuda.synchronize()
+    v = L.views()
+    rw, rids = mo.select_experts(logits.cpu(), cfg.k, cfg.renormalize)
+    perm, off, inv = mo.permutation(rids, cfg.E)
+    assert (ids.cpu().numpy() == rids).all(), "routing ids differ"
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    assert (v["expert_off"].cpu().numpy() == off).all()
+    assert (v["perm"].cpu().numpy() == perm).all()
+    assert (v["inv"].cpu().numpy() == inv).all()
+    assert L.status() == 0
+    del L
+    xc, pc, gc = x.cpu(), pool.cpu(), pages.cpu()
+    got = out.float().cpu()
+    del pool, out
+    torch.cuda.empty_cache()
+    ref = mo.stack_fused_moe(xc, pc, gc, rw, rids, rounding="fp32").float()
+    ref_r = mo.stack_fused_moe(xc, pc, gc, rw, rids, rounding="reference").float()
+    ref_err = float((ref_r - ref).abs().max())
+    ref_rel = mo.error_metrics(ref_r, ref)[1]
+    bar = max(MAX_ABS, ref_err)
+    max_abs, rel = mo.error_metrics(got, ref)
+    splits = ops.splits(cfg.E, cfg.H, cfg.I, T * cfg.k)
+    print(f"PARITY {cfg.name.split(' T')[0]} T={T} S={splits}: max_abs={max_abs:.4e} rel_l2={rel:.4e} | "
+          f"reference arithmetic vs fp32: max_abs={ref_err:.4e} rel_l2={ref_rel:.4e} | bar max_abs={bar:.4e}")
+    assert max_abs <= bar and rel <= REL_L2, f"max_abs={max_abs:.3e} (bar {bar:.3e}) rel_l2={rel:.3e}"
+
+
+@pytest.mark.parametrize("E,k,H,I,T", [
+    (1, 1, 4096, 14336, 64),   # one Mixtral-8x7B expert: 112 gate/up units < 148 SMs -> 2 K slices
+    (2, 1, 1024, 3584, 40),    # 56 gate/up units -> 4 K slices
+])
+def test_gate_up_k_slices_vs_oracle(E, k, H, I, T):
+    """Gate/up units cut into K slices (an expert-parallel rank's single expert): the
+    slices before the last store fp32 partials, the last adds them before SiLU*mul."""
+    from ae_b200 import ops
+    dev = torch.device("cuda", 0)
+    assert ops.gate_up_slices(E, H, I, T * k) > 1
+    g = torch.Generator(device=dev)
+    g.manual_seed(E * 100 + T)
+    pool = (torch.randn(E, 3 * I * H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev).to(torch.bfloat16)
+    pages = torch.arange(E, device=dev, dtype=torch.int64)
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    out = ops.moe_forward(x, logits, pool, pages, k, True, topk_ids=ids)
+    torch.cuda.synchronize()
+    rw, rids = mo.select_experts(logits.cpu(), k, True)
+    assert (ids.cpu().numpy() == rids).all()
+    xc, pc = x.cpu(), pool.cpu()
+    ref = mo.stack_fused_moe(xc, pc, pages.cpu(), rw, rids, rounding="fp32").float()
+    ref_r = mo.stack_fused_moe(xc, pc, pages.cpu(), rw, rids, rounding="reference").float()
+    bar = max(MAX_ABS, float((ref_r - ref).abs().max()))
+    max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+    print(f"PARITY K-slices E={E} H={H} I={I} T={T}: max_abs={max_abs:.4e} rel_l2={rel:.4e} bar={bar:.4e}")
+    assert max_abs <= bar and rel <= REL_L2, (max_abs, bar, rel)
+
+
+def test_prefill_sized_token_tiles_vs_oracle():
+    """512 tokens per expert: two 256-token tiles per expert, each its own unit (TMA token
+    tiles), down units per token tile."""
+    from ae_b200 import ops
+    E, k, H, I, T = 8, 2, 1024, 3584, 2048
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2048)
+    pool = (torch.randn(E, 3 * I * H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = (torch.randn(T, E, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    pages = torch.arange(E, device=dev, dtype=torch.int64)
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    out = ops.moe_forward(x, logits, pool, pages, k, True, topk_ids=ids)
+    torch.cuda.synchronize()
+    rw, rids = mo.select_experts(logits.cpu(), k, True)
+    assert (ids.cpu().numpy() == rids).all()
+    assert np.bincount(rids.reshape(-1), minlength=E).max() > 256  # several token tiles per expert
+    xc, pc = x.cpu(), pool.cpu()
+    ref = mo.stack_fused_moe(xc, pc, pages.cpu(), rw, rids, rounding="fp32").float()
+    max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+    print(f"PARITY prefill-sized E={E} H={H} I={I} T={T}: max_abs={max_abs:.4e} rel_l2={rel:.4e}")
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (max_abs, rel)
