@@ -25,7 +25,7 @@ SIGNATURES = {
     "smb_last_cuda_error": (ctypes.c_char_p, []),
     "smb_moe_workspace_bytes": (_S, [_I, _I, _I, _I, _I, _I]),
     "smb_moe_splits": (_I, [_I, _I, _I, _I]),
-    "smb_moe_gate_up_slices": (_I, [_I, _I, _I, _I]),
+    "smb_moe_ep_workspace_bytes": (_S, [_I, _I, _I, _I, _I, _I]),
     "smb_moe_route": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
     "smb_moe_permute": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "smb_moe_ffn": (_I, [_P, _P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
@@ -70,10 +70,18 @@ class Timers(ctypes.Structure):
     _fields_ = [("ffn_ns", ctypes.c_uint64), ("recv_wait_ns", ctypes.c_uint64),
                 ("combine_wait_ns", ctypes.c_uint64), ("ffn_launches", ctypes.c_uint32),
                 ("recv_waits", ctypes.c_uint32), ("combine_waits", ctypes.c_uint32),
-                ("reserved", ctypes.c_uint32)]
+                ("reserved", ctypes.c_uint32), ("stage_ns", ctypes.c_uint64 * 5),
+                ("stage_calls", ctypes.c_uint32 * 5), ("reserved2", ctypes.c_uint32),
+                ("stage_busy_ns", ctypes.c_uint64 * 5)]
+
+    STAGES = ("route", "recv_route", "ffn", "combine", "final_combine")
 
     def as_dict(self):
-        return {f[0]: int(getattr(self, f[0])) for f in self._fields_ if f[0] != "reserved"}
+        d = {f[0]: int(getattr(self, f[0])) for f in self._fields_[:6]}
+        d["stage_ns"] = {n: int(v) for n, v in zip(self.STAGES, self.stage_ns)}
+        d["stage_calls"] = {n: int(v) for n, v in zip(self.STAGES, self.stage_calls)}
+        d["stage_busy_ns"] = {n: int(v) for n, v in zip(self.STAGES, self.stage_busy_ns)}
+        return d
 
 _lock = threading.Lock()
 _lib = None

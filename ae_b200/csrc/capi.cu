@@ -112,12 +112,11 @@ int check_shape(int T, int E, int k, int H, int I, int dtype) {
   return SMB_OK;
 }
 
-// choose_plan simulates the unit queue (a few ms for the largest shapes), so its answer
-// is kept per shape.
-FfnPlan cached_plan(int E, int H, int I, int Tk, int sms) {
+// choose_splits simulates the unit queue (a few ms for the largest shapes), so its
+// answer is kept per shape.
+int cached_splits(int E, int H, int I, int Tk, int valid, int sms) {
   struct Entry {
-    int E, H, I, Tk, sms;
-    FfnPlan p;
+    int E, H, I, Tk, valid, sms, s;
   };
   constexpr int kSlots = 128;
   static Entry table[kSlots];
@@ -127,45 +126,43 @@ FfnPlan cached_plan(int E, int H, int I, int Tk, int sms) {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < used; ++i) {
       const Entry& t = table[i];
-      if (t.E == E && t.H == H && t.I == I && t.Tk == Tk && t.sms == sms) return t.p;
+      if (t.E == E && t.H == H && t.I == I && t.Tk == Tk && t.valid == valid && t.sms == sms) return t.s;
     }
   }
-  const FfnPlan p = choose_plan(E, H, I, Tk, sms);
+  const int s = choose_splits(E, H, I, Tk, sms, valid);
   std::lock_guard<std::mutex> lock(mu);
   const int slot = used < kSlots ? used++ : (next++ % kSlots);
-  table[slot] = Entry{E, H, I, Tk, sms, p};
-  return p;
+  table[slot] = Entry{E, H, I, Tk, valid, sms, s};
+  return s;
 }
 
-// The plan for these sizes on the current device.  SMB_SPLIT_K / SMB_KSPLIT_GATE_UP
-// override S / ks1 (experiments; workspaces must then be sized in the same environment).
-int plan_for(int E, int H, int I, int Tk, FfnPlan* out) {
+// Down split-K factor for these sizes on the current device; `valid` = slots expected to
+// hold a token (-1: all Tk).  SMB_SPLIT_K overrides it (experiments; workspaces must then
+// be sized in the same environment).
+int splits_for(int E, int H, int I, int Tk, int valid, int* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc != SMB_OK) return rc;
-  FfnPlan p = cached_plan(E, H, I, Tk, di.sms);
+  int s = cached_splits(E, H, I, Tk, valid, di.sms);
   const char* env = std::getenv("SMB_SPLIT_K");
   if (env != nullptr) {
     int v = std::atoi(env);
-    if (v >= 1 && v <= I / 64) p.splits = v;
+    if (v >= 1 && v <= I / 64) s = v;
   }
-  env = std::getenv("SMB_KSPLIT_GATE_UP");
-  if (env != nullptr) {
-    int v = std::atoi(env);
-    if (v == 1 || v == 2 || v == 4) p.ks1 = v;
-  }
-  *out = p;
+  *out = s;
   return SMB_OK;
 }
 
 // Carve the workspace; checks size and alignment.
-int carve(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype, WsLayout* L) {
+// `valid`: slots expected to hold a token (-1: all), the expert side of the exchange.
+int carve(const void* ws, size_t ws_bytes, int T, int E, int k, int H, int I, int dtype, WsLayout* L,
+          int valid = -1) {
   int rc = check_shape(T, E, k, H, I, dtype);
   if (rc != SMB_OK) return rc;
-  FfnPlan plan;
-  rc = plan_for(E, H, I, T * k, &plan);
+  int s = 1;
+  rc = splits_for(E, H, I, T * k, valid, &s);
   if (rc != SMB_OK) return rc;
-  *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), plan);
+  *L = make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s);
   if (ws == nullptr) return SMB_ERR_NULL;
   if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
   if (ws_bytes < L->total) return SMB_ERR_WORKSPACE;
@@ -176,6 +173,9 @@ template <typename P>
 P* at(const void* ws, size_t off) {
   return reinterpret_cast<P*>(reinterpret_cast<uintptr_t>(ws) + off);
 }
+
+// Stage clock of the control block at `ctrl` (a workspace, or an exchange arena).
+StageClock* clock_at(const void* ctrl) { return at<StageClock>(ctrl, kStageOffset); }
 
 // Small cache of encoded tensor maps: a layer is called with the same pool and
 // workspace over and over, and encoding costs microseconds of host time per map.
@@ -305,7 +305,8 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
              size_t ws_bytes, cudaStream_t stream, const EpLayout& ep = EpLayout(), const GateIn* gate = nullptr,
              const SharedIn& shared = SharedIn()) {
   WsLayout L;
-  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  // the expert side of the exchange: about C of its G x C slots hold a token
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L, ep.recv != nullptr ? ep.C : -1);
   if (rc != SMB_OK) return rc;
   if (logits != nullptr && logits_dtype != SMB_DTYPE_F16 && logits_dtype != SMB_DTYPE_BF16 &&
       logits_dtype != SMB_DTYPE_F32)
@@ -352,6 +353,9 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.ep_C = ep.C;
   a.ep_Eloc = ep.Eloc;
   a.link = ep.link;
+  // over peer memory the whole exchange chain stamps the arena's clock
+  a.clk = ep.link.p2p ? clock_at(ep.link.ctrl) : clock_at(ws);
+  a.stage = ep.recv != nullptr ? 1 : 0;
   const int Tk = T * k;
   if (gate != nullptr) {
     // gate + routing in one launch: the gate's CTAs each take ceil(T / SMs) tokens, the
@@ -382,9 +386,10 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
 // run both phases in one persistent launch.
 int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
            int T, int E, int k, int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases,
-           bool counters_zeroed, const int* page_ready = nullptr, int page_epoch = 0) {
+           bool counters_zeroed, const int* page_ready = nullptr, int page_epoch = 0, StageClock* clk = nullptr,
+           const EpLink* out_link = nullptr) {
   WsLayout L;
-  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L, x_chunk > 0 ? x_chunk : -1);
   if (rc != SMB_OK) return rc;
   if (T == 0) return SMB_OK;
   if (pool == nullptr || page_of_expert == nullptr) return SMB_ERR_NULL;
@@ -413,11 +418,7 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.status = at<int>(ws, L.status);
   args.sched = at<int>(ws, L.done);
   args.done = args.sched + 2;
-  args.fix = args.done + static_cast<size_t>(E) * L.splits * L.ntc;
-  args.gu = at<float>(ws, L.gu);
-  args.ks1 = L.ks1;
   args.ntc = L.ntc;
-  args.rows = L.rows;
   args.x = x;
   args.x_chunk = x_chunk;
   args.inv = at<int32_t>(ws, L.inv);
@@ -434,6 +435,14 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.page_epoch = page_epoch;
   args.splits = L.splits;
   args.phase_mask = phases;
+  args.clk = clk != nullptr ? clk : clock_at(ws);
+  args.tile_done = args.done + static_cast<size_t>(E) * L.splits * L.ntc;
+  args.perm = at<int32_t>(ws, L.perm);
+  if (out_link != nullptr) {
+    // expert side of the exchange: the FFN writes the returned rows itself
+    args.ep_C = x_chunk;
+    args.link = *out_link;
+  }
   if (!counters_zeroed) {
     // standalone call: the router zeroed the counters for the first FFN launch only
     cudaError_t err = cudaMemsetAsync(args.sched, 0, sizeof(int) * static_cast<size_t>(L.ndone), stream);
@@ -444,13 +453,13 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
 }
 
 int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const void* ws, size_t ws_bytes,
-               cudaStream_t stream, int ep_C = 0, const EpLink* link = nullptr) {
+               cudaStream_t stream) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
   if (T == 0) return SMB_OK;
-  if (ep_C == 0 && out == nullptr) return SMB_ERR_NULL;  // the expert side writes through link->chunk
-  if (out != nullptr && !aligned(out, 16)) return SMB_ERR_ALIGN;
+  if (out == nullptr) return SMB_ERR_NULL;
+  if (!aligned(out, 16)) return SMB_ERR_ALIGN;
   CombineArgs a{};
   a.part = at<const float>(ws, L.part);
   a.inv = at<const int32_t>(ws, L.inv);
@@ -460,8 +469,7 @@ int do_combine(void* out, int dtype, int T, int E, int k, int H, int I, const vo
   a.k = k;
   a.H = H;
   a.splits = L.splits;
-  a.ep_C = ep_C;
-  if (link != nullptr) a.link = *link;
+  a.clk = clock_at(ws);
   cudaError_t err = launch_combine(a, dtype == SMB_DTYPE_BF16, stream, pdl_enabled());
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
@@ -513,23 +521,25 @@ const char* smb_last_cuda_error(void) { return g_last_cuda_error; }
 
 size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dtype) {
   if (check_shape(T, E, k, H, I, dtype) != SMB_OK) return 0;
-  FfnPlan plan;
-  if (plan_for(E, H, I, T * k, &plan) != SMB_OK) return 0;
-  return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), plan).total;
+  int s = 1;
+  if (splits_for(E, H, I, T * k, -1, &s) != SMB_OK) return 0;
+  return make_ws_layout(T, E, k, H, I, elem_bytes_of(dtype), s).total;
+}
+
+size_t smb_moe_ep_workspace_bytes(int G, int C, int E_loc, int H, int I, int dtype) {
+  if (G < 1 || G > kMaxRanks || C < 1) return 0;
+  const int T = G * C;
+  if (check_shape(T, E_loc, 1, H, I, dtype) != SMB_OK) return 0;
+  int s = 1;
+  if (splits_for(E_loc, H, I, T, C, &s) != SMB_OK) return 0;
+  return make_ws_layout(T, E_loc, 1, H, I, elem_bytes_of(dtype), s).total;
 }
 
 int smb_moe_splits(int E, int H, int I, int Tk) {
   if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0 || Tk < 0) return SMB_ERR_SHAPE;
-  FfnPlan plan;
-  int rc = plan_for(E, H, I, Tk, &plan);
-  return rc == SMB_OK ? plan.splits : rc;
-}
-
-int smb_moe_gate_up_slices(int E, int H, int I, int Tk) {
-  if (E < 1 || H < 128 || H % 128 != 0 || I < 64 || I % 64 != 0 || Tk < 0) return SMB_ERR_SHAPE;
-  FfnPlan plan;
-  int rc = plan_for(E, H, I, Tk, &plan);
-  return rc == SMB_OK ? plan.ks1 : rc;
+  int s = 1;
+  int rc = splits_for(E, H, I, Tk, -1, &s);
+  return rc == SMB_OK ? s : rc;
 }
 
 int smb_moe_route(const void* router_logits, int logits_dtype, const void* x, int dtype, int T, int E, int k,
@@ -580,7 +590,7 @@ int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, i
   if (!aligned(rows, 16) || !aligned(out, 16)) return SMB_ERR_ALIGN;
   cudaError_t err = launch_combine_rows(rows, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
                                         dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
-                                        pdl_enabled());
+                                        pdl_enabled(), nullptr, nullptr, 0, 1, nullptr, nullptr, clock_at(ws));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -624,18 +634,17 @@ int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t
   ep.G = G;
   ep.C = C;
   ep.Eloc = E_loc;
+  if (G > kMaxRanks) return SMB_ERR_SHAPE;
   int rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
                     ws_bytes, s, ep);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
-  if (rc != SMB_OK) return rc;
-  if (G > kMaxRanks) return SMB_ERR_SHAPE;
   EpLink link{};
   link.nranks = G;
   for (int src = 0; src < G; ++src) {
     link.chunk[src] = static_cast<uint8_t*>(out_rows) + static_cast<size_t>(src) * C * H * elem_bytes_of(dtype);
   }
-  return do_combine(out_rows, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, C, &link);
+  return do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true, nullptr,
+                0, nullptr, &link);
 }
 
 size_t smb_ep_arena_bytes(int G, int C, int H, int dtype) {
@@ -737,8 +746,6 @@ int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const vo
   rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
                 ws_bytes, s, ep);
   if (rc != SMB_OK) return rc;
-  rc = do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true);
-  if (rc != SMB_OK) return rc;
   EpLink link{};
   link.nranks = G;
   link.p2p = 1;
@@ -747,7 +754,9 @@ int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const vo
     link.chunk[src] = P.arena[src] + P.A.back + static_cast<size_t>(rank) * C * P.row_bytes;
     link.flag[src] = ep_flags(P, src) + kEpReturnFlags + rank;
   }
-  return do_combine(nullptr, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, C, &link);
+  // the FFN kernel writes every row's output into its source's arena and raises the flags
+  return do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true, nullptr,
+                0, clock_at(ep_ctrl(P, rank)), &link);
 }
 
 int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int I, int G, int rank, int C,
@@ -771,7 +780,7 @@ int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int
                                         at<const float>(ws, L.w), out, T, k, H, dtype == SMB_DTYPE_BF16,
                                         reinterpret_cast<cudaStream_t>(stream), pdl_enabled(),
                                         at<const int32_t>(ws, L.ids), at<const int32_t>(ws, L.expert_off), C, E / G,
-                                        &link, at<int>(ws, L.status));
+                                        &link, at<int>(ws, L.status), clock_at(ep_ctrl(P, rank)));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -787,7 +796,8 @@ int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int
   cudaError_t err = launch_combine_rows(back, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
                                         dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
                                         pdl_enabled(), at<const int32_t>(ws, L.ids),
-                                        at<const int32_t>(ws, L.expert_off), C, E / G);
+                                        at<const int32_t>(ws, L.expert_off), C, E / G, nullptr, nullptr,
+                                        clock_at(ws));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -958,18 +968,28 @@ int smb_moe_read_timers(const void* ws, size_t ws_bytes, int reset, smb_timers_t
   if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
   if (ws_bytes < kWsHeaderBytes) return SMB_ERR_WORKSPACE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  DevTimers h{};
+  struct {
+    DevTimers t;
+    StageClock c;
+  } h{};
+  static_assert(kStageOffset == kTimerOffset + sizeof(DevTimers), "timers then stage clock");
   const void* src = at<const void>(ws, kTimerOffset);
   cudaError_t err = cudaMemcpyAsync(&h, src, sizeof(h), cudaMemcpyDeviceToHost, s);
   if (err == cudaSuccess) err = cudaStreamSynchronize(s);
   if (err == cudaSuccess && reset) err = cudaMemsetAsync(const_cast<void*>(src), 0, sizeof(h), s);
   if (err != cudaSuccess) return cuda_fail(err);
-  out->ffn_ns = h.ffn_ns;
-  out->recv_wait_ns = h.recv_wait_ns;
-  out->combine_wait_ns = h.combine_wait_ns;
-  out->ffn_launches = h.ffn_launches;
-  out->recv_waits = h.recv_waits;
-  out->combine_waits = h.combine_waits;
+  for (int i = 0; i < kStages; ++i) {
+    out->stage_ns[i] = h.c.ns[i];
+    out->stage_calls[i] = h.c.n[i];
+    out->stage_busy_ns[i] = h.c.busy[i];
+  }
+  DevTimers& t = h.t;
+  out->ffn_ns = t.ffn_ns;
+  out->recv_wait_ns = t.recv_wait_ns;
+  out->combine_wait_ns = t.combine_wait_ns;
+  out->ffn_launches = t.ffn_launches;
+  out->recv_waits = t.recv_waits;
+  out->combine_waits = t.combine_waits;
   out->reserved = 0;
   return SMB_OK;
 }

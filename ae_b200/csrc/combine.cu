@@ -21,7 +21,6 @@ constexpr int kCombineThreads = 256;
 template <typename TO>
 __device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4) {
   const size_t Tk = static_cast<size_t>(a.T) * a.k;
-  if (a.ep_C > 0 && a.inv[t] < 0) return;  // expert side of the exchange: an empty payload slot
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < a.k; ++j) {
     const size_t f = static_cast<size_t>(t) * a.k + j;
@@ -57,15 +56,7 @@ __device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4)
     acc.z += wj * s.z;
     acc.w += wj * s.w;
   }
-  TO* out;
-  if (a.ep_C > 0) {
-    // row t = s*C + i of the exchange goes back to source s (local buffer for NCCL, the
-    // source's return buffer over peer memory)
-    const int s = t / a.ep_C;
-    out = reinterpret_cast<TO*>(a.link.chunk[s]) + static_cast<size_t>(t - s * a.ep_C) * a.H;
-  } else {
-    out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H;
-  }
+  TO* out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H;
   union {
     TO h[4];
     uint2 u;
@@ -80,19 +71,11 @@ __device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4)
 template <typename TO>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
   pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) stage_mark(a.clk, 3);
   pdl_launch_dependents();
   const int t = blockIdx.y;
   const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
   if (h4 * 4 < a.H) combine_one<TO>(a, t, h4);
-  // over peer memory: when every row has been sent, raise this rank's return flag at
-  // each source
-  if (a.link.p2p) {
-    __shared__ int s_last;
-    if (last_cta_of_grid(a.link.ctrl + 2, &s_last) && threadIdx.x == 0) {
-      const int epoch = a.link.ctrl[0] + 1;
-      for (int s = 0; s < a.link.nranks; ++s) st_release_sys(a.link.flag[s], epoch);
-    }
-  }
 }
 
 template <typename TO>
@@ -144,8 +127,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
                                                                         const float* w, void* out_v, int T, int k,
                                                                         int H, const int32_t* ids,
                                                                         const int32_t* expert_off, int ep_C,
-                                                                        int ep_Eloc, const EpLink link, int* status) {
+                                                                        int ep_Eloc, const EpLink link, int* status,
+                                                                        StageClock* clk) {
   pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) stage_mark(clk, 4);
   pdl_launch_dependents();
   const int t = blockIdx.y;
   const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
@@ -166,7 +151,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const voi
   if (h4 * 4 < H && t < T) combine_rows_one<TO>(rows_v, inv, w, out_v, T, k, H, ids, expert_off, ep_C, ep_Eloc, t, h4);
   if (link.p2p) {
     // every CTA has read its rows: this call is finished on this rank, advance the epoch
-    if (last_cta_of_grid(link.ctrl + 3, &s_last) && threadIdx.x == 0) link.ctrl[0] = link.ctrl[0] + 1;
+    if (last_cta_of_grid(link.ctrl + 3, &s_last) && threadIdx.x == 0) {
+      link.ctrl[0] = link.ctrl[0] + 1;
+      stage_busy(clk, 4);
+    }
   }
 }
 
@@ -245,7 +233,7 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
                                 int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids,
                                 const int32_t* expert_off, int ep_C, int ep_Eloc, const EpLink* link,
-                                int* status) {
+                                int* status, StageClock* clk) {
   EpLink lk{};
   if (link != nullptr) lk = *link;
   const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_rows_kernel<__nv_bfloat16>)
@@ -261,7 +249,7 @@ cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const floa
   cfg.numAttrs = 1;
   void* params[] = {const_cast<void**>(&rows), const_cast<int32_t**>(&inv), const_cast<float**>(&w), &out, &T,
                     &k, &H, const_cast<int32_t**>(&ids), const_cast<int32_t**>(&expert_off), &ep_C, &ep_Eloc,
-                    &lk, &status};
+                    &lk, &status, &clk};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

@@ -88,13 +88,41 @@ __device__ __forceinline__ void add_wait_time(unsigned long long* sum, unsigned 
   atomicAdd(count, 1u);
 }
 
+// Stage clock of the control block whose first byte is `ctrl`.
+__device__ __forceinline__ StageClock* stage_clock_of(void* ctrl) {
+  return reinterpret_cast<StageClock*>(reinterpret_cast<uint8_t*>(ctrl) + kStageOffset);
+}
+
+// Called by one thread of block 0, after the kernel's wait on its predecessor.
+__device__ __forceinline__ void stage_mark(StageClock* c, int stage) {
+  if (c == nullptr) return;
+  const unsigned long long t = global_timer_ns();
+  const unsigned long long last = c->last;
+  const unsigned int prev = c->last_stage;
+  if (last != 0 && t > last && prev < static_cast<unsigned int>(kStages)) {
+    c->ns[prev] += t - last;
+    c->n[prev] += 1u;
+  }
+  c->last = t;
+  c->last_stage = static_cast<unsigned int>(stage);
+}
+
+// Called by one thread once the stage's kernel has done its work (the last CTA of the
+// grid): adds the time since the stage's stamp to its busy time.
+__device__ __forceinline__ void stage_busy(StageClock* c, int stage) {
+  if (c == nullptr || c->last_stage != static_cast<unsigned int>(stage) || c->last == 0) return;
+  const unsigned long long t = global_timer_ns();
+  if (t > c->last) c->busy[stage] += t - c->last;
+}
+
 // Kernel-duration timer of a grid: every CTA calls begin once (after its dependency
 // wait) and end once (after its last store); the CTA that ends last adds the span from
 // the earliest begin to its end.  One thread per CTA calls them.
 __device__ __forceinline__ void grid_timer_begin(DevTimers* tm) {
   atomicMax(&tm->ffn_neg_t0, ~0ull - static_cast<unsigned long long>(global_timer_ns()));
 }
-__device__ __forceinline__ void grid_timer_end(DevTimers* tm) {
+// True in the CTA that ended last.
+__device__ __forceinline__ bool grid_timer_end(DevTimers* tm) {
   __threadfence();
   const unsigned int n = gridDim.x * gridDim.y * gridDim.z;
   if (atomicAdd(&tm->ffn_exit, 1u) == n - 1) {
@@ -103,7 +131,9 @@ __device__ __forceinline__ void grid_timer_end(DevTimers* tm) {
     atomicAdd(&tm->ffn_ns, t1 > t0 ? t1 - t0 : 0ull);
     atomicAdd(&tm->ffn_launches, 1u);
     atomicExch(&tm->ffn_exit, 0u);
+    return true;
   }
+  return false;
 }
 
 // ---------------------------------------------------------------- mbarrier

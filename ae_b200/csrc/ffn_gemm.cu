@@ -122,7 +122,6 @@ struct Unit {
   int te;     // index into the touched-expert list
   int mt;     // 128-feature tile (phase 1) or 256-row tile of w2 (phase 2)
   int nt;     // token tile of the expert (ncap tokens each)
-  int kq;     // K slice of a gate/up unit (phase 1)
   int ks;     // split index (phase 2)
   int kb0;    // first 64-wide K block
   int kb1;    // one past the last K block
@@ -133,7 +132,6 @@ struct Geometry {
   int m1, m2;         // tiles per expert
   int kb1_total, kb2_total;
   int splits;         // down split-K factor S
-  int ks1;            // gate/up K slices
   const int* ntp;     // [touched + 1] prefix of token tiles over the touched experts (shared memory)
   int ntouched;
 };
@@ -148,25 +146,22 @@ __device__ __forceinline__ int expert_of_tile(const Geometry& g, int q) {
   return lo;
 }
 
-// Unit order: all gate/up units, expert by expert, then feature tile, token tile and K
-// slice; then all down units, expert by expert, then split, row tile and token tile.
+// Unit order: all gate/up units, expert by expert, then feature tile and token tile; then
+// all down units, expert by expert, then split, row tile and token tile.
 // Units that stream the same weight rows for different token tiles are adjacent, so they
 // are claimed at about the same time and the later ones read the rows from L2.
 __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
   Unit r;
   if (u < g.n1) {
-    const int per_tile = g.m1 * g.ks1;  // units per token tile of an expert
     r.phase = 1;
-    r.te = expert_of_tile(g, u / per_tile);
+    r.te = expert_of_tile(g, u / g.m1);
     const int nte = g.ntp[r.te + 1] - g.ntp[r.te];
-    const int v = u - g.ntp[r.te] * per_tile;
-    r.mt = v / (nte * g.ks1);
-    const int q = v - r.mt * nte * g.ks1;
-    r.nt = q / g.ks1;
-    r.kq = q - r.nt * g.ks1;
+    const int v = u - g.ntp[r.te] * g.m1;
+    r.mt = v / nte;
+    r.nt = v - r.mt * nte;
     r.ks = 0;
-    r.kb0 = static_cast<int>((static_cast<long long>(g.kb1_total) * r.kq) / g.ks1);
-    r.kb1 = static_cast<int>((static_cast<long long>(g.kb1_total) * (r.kq + 1)) / g.ks1);
+    r.kb0 = 0;
+    r.kb1 = g.kb1_total;
   } else {
     // expert-major like the gate/up units, then split: an expert's first down units read
     // only its first features, whose gate/up units finish first
@@ -180,7 +175,6 @@ __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
     const int q = v - r.ks * g.m2 * nte;
     r.mt = q / nte;
     r.nt = q - r.mt * nte;
-    r.kq = 0;
     r.kb0 = static_cast<int>((static_cast<long long>(g.kb2_total) * r.ks) / g.splits);
     r.kb1 = static_cast<int>((static_cast<long long>(g.kb2_total) * (r.ks + 1)) / g.splits);
   }
@@ -233,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_page[kMaxExperts];
   __shared__ int s_ntp[kMaxExperts + 1];
   __shared__ int s_ntouched, s_ncap, s_stages;
-  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed;
+  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_epi_last, s_issued, s_consumed, s_last_cta;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -244,7 +238,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool do1 = (args.phase_mask & 1) != 0;
   const bool do2 = (args.phase_mask & 2) != 0;
   const bool chained = do1 && do2;  // phase 2 waits on this launch's phase 1
-  const int ks1 = do1 ? args.ks1 : 1;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -282,18 +275,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // never waited on.  page_of_expert was written before the router started, so it is final.
   if (threadIdx.x == 0 && do1 && args.page_ready == nullptr) {
     const int m1 = (I + 127) / 128;
-    const int unit = static_cast<int>(blockIdx.x);
-    const int e = unit / (m1 * ks1);
-    const int mt = (unit / ks1) % m1;
-    const int kq = unit % ks1;
+    const int e = static_cast<int>(blockIdx.x) / m1;
     if (e < E) {
       const long long pg = args.page_of_expert[e];
       if (pg >= 0 && pg < args.num_pages) {
-        const int r0 = static_cast<int>(pg) * 3 * I + mt * 128;
-        const int kbt = H / kBK;
-        const int kb0 = kbt * kq / ks1;
-        const int kbs = min(kbt * (kq + 1) / ks1 - kb0, kPrefetchBlocks);
-        for (int kb = kb0; kb < kb0 + kbs; ++kb) {
+        const int r0 = static_cast<int>(pg) * 3 * I + (static_cast<int>(blockIdx.x) % m1) * 128;
+        const int kbs = min(H / kBK, kPrefetchBlocks);
+        for (int kb = 0; kb < kbs; ++kb) {
           tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0);
           tma_prefetch_l2_2d(&tm_w13, kb * kBK, r0 + I);
         }
@@ -305,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // hints); the routing results and the token rows come from the router.
   pdl_wait_prior_grids();
   if (threadIdx.x == 0) grid_timer_begin(timers_of(args.status));
+  if (threadIdx.x == 0 && blockIdx.x == 0) stage_mark(args.clk, 2);
 
   if (threadIdx.x == 0) {
     int nt = 0, maxn = 0;
@@ -383,11 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   g.kb1_total = H / kBK;
   g.kb2_total = I / kBK;
   g.splits = args.splits;
-  g.ks1 = ks1;
   g.ntp = s_ntp;
   g.ntouched = s_ntouched;
   const int tiles = s_ntp[s_ntouched];
-  g.n1 = do1 ? tiles * g.m1 * g.ks1 : 0;
+  g.n1 = do1 ? tiles * g.m1 : 0;
   g.n2 = do2 ? tiles * g.m2 * g.splits : 0;
   g.total = g.n1 + g.n2;
 
@@ -632,7 +620,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // A2 rows are read back by the down units and the partials by the combine moments
     // later; keep them in L2 while the weight stream (evict-first) passes through
     const uint64_t pol_keep = policy_evict_last();
-    const size_t gu_slice = static_cast<size_t>(args.rows) * 2 * I;  // floats per gate/up K slice
     int qi = 0;
     uint32_t qph = 0;
     int pass = 0;
@@ -649,15 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int row0, n0, nlen;
       tile_tokens(un, row0, n0, nlen);
       const int buf = pass % nbuf;
-      // a gate/up unit cut into K slices: the last slice adds the others' stored partials
-      const bool slice_store = un.phase == 1 && ks1 > 1 && un.kq < ks1 - 1;
-      const bool slice_sum = un.phase == 1 && ks1 > 1 && un.kq == ks1 - 1;
-      const int fixc = (e * g.m1 + un.mt) * args.ntc + un.nt;  // K-slice counter of this tile
-      if (et == 0) {
-        bool okw = mbar_wait(&tfull_bar[buf], (pass / nbuf) & 1, args.status, &s_abort);
-        if (okw && slice_sum) okw = wait_count(args.fix + fixc, ks1 - 1, args.status, &s_abort);
-        s_epi_ok = okw ? 1 : 0;
-      }
+      if (et == 0) s_epi_ok = mbar_wait(&tfull_bar[buf], (pass / nbuf) & 1, args.status, &s_abort) ? 1 : 0;
       named_bar_sync(1, 128);
       ok = s_epi_ok != 0;
       named_bar_sync(1, 128);
@@ -669,41 +648,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // vectors along the row (8 activations or 4 partials per store) instead of one
       // element per thread per token.
       uint8_t* stg = dyn_smem + (kDynSmem - kEpiStage) + sub * 2048;
-      const int feat = un.mt * 128 + sub * 32 + lane;  // gate/up feature of this thread's TMEM lane
       for (int c0 = 0; c0 < nlen; c0 += 16) {
         float va[16], vb[16];
         tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
         tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
         const int nt = min(16, nlen - c0);
-        // this thread's element of token row row0 + n0 + c0 in a gate/up slice [rows, 2I]
-        const size_t gu_at = static_cast<size_t>(row0 + n0 + c0) * 2 * I + feat;
-        const int nrow = feat < I ? nt : 0;
-        if (slice_store) {
-          // fp32 gate and up partial sums of this K slice: lanes of a warp write 32
-          // consecutive features of one token row (128 B) per store
-          float* dst = args.gu + static_cast<size_t>(un.kq) * gu_slice + gu_at;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (i < nrow) {
-              dst[0] = va[i];
-              dst[I] = vb[i];
-            }
-            dst += 2 * I;
-          }
-        } else if (un.phase == 1) {
-          if (slice_sum) {
-            for (int q = 0; q < ks1 - 1; ++q) {
-              const float* src = args.gu + static_cast<size_t>(q) * gu_slice + gu_at;
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                if (i < nrow) {
-                  va[i] += __ldcg(src);
-                  vb[i] += __ldcg(src + I);
-                }
-                src += 2 * I;
-              }
-            }
-          }
+        if (un.phase == 1) {
           T* st = reinterpret_cast<T*>(stg);
 #pragma unroll
           for (int i = 0; i < 16; ++i) st[i * 32 + lane] = from_f32<T>(silu_f32(va[i]) * vb[i]);
@@ -744,11 +694,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty_bar[buf]);
       ++pass;
-      if (slice_store) {
-        // publish this K slice's partials (release at GPU scope) to the tile's last slice
+      if (un.phase == 2 && args.ep_C > 0) {
+        // expert side of the exchange: publish this unit's partials; the unit that
+        // completes the output tile (all S splits stored) sums them in split order and
+        // writes each row to its source's chunk in the storage dtype
         __threadfence();
         named_bar_sync(1, 128);
-        if (et == 0) atomicAdd(args.fix + fixc, 1);
+        if (et == 0) {
+          const int old = atomicAdd(args.tile_done + (e * g.m2 + un.mt) * args.ntc + un.nt, 1);
+          s_epi_last = old == g.splits - 1 ? 1 : 0;
+          __threadfence();
+        }
+        named_bar_sync(1, 128);
+        if (s_epi_last) {
+          const int h0 = un.mt * 256;
+          const int nh4 = min(256, H - h0) / 4;  // float4 per row of the tile
+          for (int idx = et; idx < nlen * nh4; idx += 128) {
+            const int r = idx / nh4, c4 = idx - r * nh4;
+            const int p = row0 + n0 + r;
+            const int h = h0 + c4 * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < g.splits; ++sp) {
+              const float4 v =
+                  __ldcg(reinterpret_cast<const float4*>(args.part + (static_cast<size_t>(sp) * args.Tk + p) * H + h));
+              acc.x += v.x;
+              acc.y += v.y;
+              acc.z += v.z;
+              acc.w += v.w;
+            }
+            const int f = args.perm[p];
+            if (f < 0 || f >= args.Tk) continue;
+            const int src = f / args.ep_C;
+            const int i = f - src * args.ep_C;
+            union {
+              T h[4];
+              uint2 u;
+            } pk;
+            pk.h[0] = from_f32<T>(acc.x);
+            pk.h[1] = from_f32<T>(acc.y);
+            pk.h[2] = from_f32<T>(acc.z);
+            pk.h[3] = from_f32<T>(acc.w);
+            *reinterpret_cast<uint2*>(reinterpret_cast<T*>(args.link.chunk[src]) + static_cast<size_t>(i) * H + h) =
+                pk.u;
+          }
+        }
       } else if (un.phase == 1 && chained) {
         // publish: this tile's A2 columns are written (release at GPU scope); count it
         // for every down split whose K range overlaps its 128 features
@@ -786,7 +775,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-  if (threadIdx.x == 0) grid_timer_end(timers_of(args.status));
+  if (args.ep_C > 0 && args.link.p2p) {
+    // every CTA's returned rows are stored into the sources' arenas: the last CTA raises
+    // each source's return flag (also after a failed wait, so that no peer stalls)
+    if (last_cta_of_grid(args.link.ctrl + 2, &s_last_cta) && threadIdx.x == 0) {
+      const int epoch = args.link.ctrl[0] + 1;
+      for (int src = 0; src < args.link.nranks; ++src) st_release_sys(args.link.flag[src], epoch);
+    }
+  }
+  if (threadIdx.x == 0 && grid_timer_end(timers_of(args.status))) stage_busy(args.clk, 2);
 }
 
 // ---------------------------------------------------------------- host side

@@ -28,36 +28,6 @@ inline cudaError_t ensure_dyn_smem(const void* fn, int bytes, std::atomic<int>* 
   return err;
 }
 
-struct FfnArgs {
-  const int32_t* expert_off;      // [E+1]
-  const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
-  int* status;                    // device status word
-  int* done;                      // [E*S*ntc] finished gate/up tiles per (expert, down split, token tile)
-  int* fix;                       // [E*m1*ntc] gate/up K slices stored per (expert, feature tile, token tile)
-  int* sched;                     // [2] next unit to hand out, CTAs done gathering (all zeroed by the router)
-  float* gu;                      // [ks1-1, rows, 2I] gate/up partials of the K slices before the last
-  int ks1;                        // gate/up K slices (1: none)
-  int ntc;                        // token-tile bound per expert (counter stride)
-  int rows;                       // rows of xp / a2 / each gu slice
-  const void* x;                  // token rows: the layer input [T, H], or the exchange layout
-  int x_chunk;                    // 0: row t of x; C > 0: payload row t of [G][C+1][H]
-  const int32_t* inv;             // [Tk] expert-major position of each flat slot
-  int k;                          // top-k (slot f belongs to token f / k)
-  void* xp;                       // [rows, H] gathered token rows, expert-major
-  void* a2;                       // [rows, I] activations, expert-major
-  float* part;                    // [S, Tk, H] split-K partials of the down projection
-  long long num_pages;            // P
-  int E, H, I, Tk, splits;
-  int phase_mask;                 // 1: gate/up, 2: down, 3: both in one launch
-  // streamed expert pages: page p's weights are usable once page_ready[p] >= page_epoch
-  // (raised by the copy stream after the page's host-to-device copy); nullptr: resident
-  const int* page_ready;
-  int page_epoch;
-};
-
-cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
-                            const CUtensorMap& w2, const CUtensorMap& xp, const CUtensorMap& a2, const FfnArgs& args);
-
 // Expert-parallel exchange over peer memory.  Rank r's arena (same layout on every rank,
 // mapped by its peers through CUDA IPC) holds a control block (epoch, CTA tickets), the
 // flags its peers set, and the receive / return chunks.  chunk[d] is where this kernel
@@ -72,6 +42,42 @@ struct EpLink {
   int nranks;
   int p2p;                 // 1: peer memory with flags, 0: NCCL moves the buffers
 };
+
+struct FfnArgs {
+  const int32_t* expert_off;      // [E+1]
+  const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
+  int* status;                    // device status word
+  int* done;                      // [E*S*ntc] finished gate/up tiles per (expert, down split, token tile)
+  int* sched;                     // [2] next unit to hand out, CTAs done gathering (all zeroed by the router)
+  int ntc;                        // token-tile bound per expert (counter stride)
+  const void* x;                  // token rows: the layer input [T, H], or the exchange layout
+  int x_chunk;                    // 0: row t of x; C > 0: payload row t of [G][C+1][H]
+  const int32_t* inv;             // [Tk] expert-major position of each flat slot
+  int k;                          // top-k (slot f belongs to token f / k)
+  void* xp;                       // [rows, H] gathered token rows, expert-major
+  void* a2;                       // [rows, I] activations, expert-major
+  float* part;                    // [S, Tk, H] split-K partials of the down projection
+  long long num_pages;            // P
+  int E, H, I, Tk, splits;
+  int phase_mask;                 // 1: gate/up, 2: down, 3: both in one launch
+  // streamed expert pages: page p's weights are usable once page_ready[p] >= page_epoch
+  // (raised by the copy stream after the page's host-to-device copy); nullptr: resident
+  const int* page_ready;
+  int page_epoch;
+  StageClock* clk;                // stage clock of the call's chain (stage 2), or nullptr
+  // Expert side of the exchange (ep_C > 0): the down units of an output tile (256 rows of
+  // H x one token tile) count themselves in tile_done; the one that completes the tile
+  // sums its rows' S split partials in split order and writes the sums, in the storage
+  // dtype, to row f % C of chunk f / C of `link` (f = perm[p], the slot of position p).
+  // Over peer memory the grid's last CTA then raises each source's return flag.
+  int* tile_done;                 // [E*m2*ntc] finished down units per (expert, row tile, token tile)
+  const int32_t* perm;            // [Tk] slot of each expert-major position
+  int ep_C;                       // C, or 0: partials only (the combine kernel reduces them)
+  EpLink link;
+};
+
+cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
+                            const CUtensorMap& w2, const CUtensorMap& xp, const CUtensorMap& a2, const FfnArgs& args);
 
 struct RouteArgs {
   const void* logits;      // [T, E] or nullptr (routing given)
@@ -100,6 +106,8 @@ struct RouteArgs {
   const void* ep_recv;     // receive: tokens are the payload rows, ids come from the headers
   int ep_G, ep_C, ep_Eloc;
   EpLink link;
+  StageClock* clk;         // stage clock of the call's chain, or nullptr
+  int stage;               // 0 routing / dispatch, 1 expert-side receive routing
 };
 
 // Router gate fused with the routing (gate_route_kernel): logits = x W^T of
@@ -128,10 +136,7 @@ struct CombineArgs {
   const float* w;       // [Tk]
   void* out;            // [T, H] storage dtype
   int T, k, H, splits;
-  // expert side of the exchange (ep_C > 0): row t = s*C + i goes to link.chunk[s] + i rows;
-  // rows without a slot are skipped
-  int ep_C;
-  EpLink link;
+  StageClock* clk;      // stage clock of the call's chain (stage 3), or nullptr
 };
 
 cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream, bool pdl);
@@ -141,7 +146,7 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
                                 int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids = nullptr,
                                 const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1,
-                                const EpLink* link = nullptr, int* status = nullptr);
+                                const EpLink* link = nullptr, int* status = nullptr, StageClock* clk = nullptr);
 
 // Host helpers of the C ABI shared with the other entry-point files: record a CUDA error
 // for smb_last_cuda_error (returns SMB_ERR_CUDA), and read a device status word as an

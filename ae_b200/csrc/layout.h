@@ -44,19 +44,28 @@ struct DevTimers {
 static_assert(sizeof(DevTimers) == 48, "timer block layout");
 static_assert(kTimerOffset + sizeof(DevTimers) <= 256, "timer block inside the control block");
 
-// How the FFN kernel cuts a layer call into units of work (host-chosen, a pure function
-// of the sizes and the SM count, so that workspace sizing and launches agree):
-//   splits  S: split-K factor of the down projection;
-//   ks1:       split-K factor of the gate/up projection, > 1 only when there are fewer
-//              gate/up units than SMs (one expert on a rank of an expert-parallel layer);
-//              slices before the last store fp32 partials that the last slice adds
-//   ntc:       bound on token tiles per expert (an expert with more than 256 tokens is
-//              cut into tiles of 256, each its own unit)
-struct FfnPlan {
-  int splits = 1;
-  int ks1 = 1;
+// Stage clock of a chain of kernels (one layer call), after the timers in the same control
+// block (a workspace's, or an exchange arena's for the peer-memory expert-parallel layer):
+// block 0 of each kernel, once past its wait on the previous kernel, charges the time
+// since the previous kernel's stamp to that kernel's stage and stamps itself.  Kernels of
+// a chain run one after another, so plain loads and stores suffice.  Stages: 0 routing
+// (or the expert-parallel dispatch), 1 expert-side receive routing, 2 FFN, 3 combine (the
+// expert-side combine of the exchange), 4 source-side final combine.  The last stage of a
+// call is charged when the next call starts.
+constexpr int kStages = 5;
+constexpr size_t kStageOffset = kTimerOffset + sizeof(DevTimers);
+struct StageClock {
+  unsigned long long last;        // %globaltimer of the last stamp (0: none yet)
+  unsigned int last_stage;        // the stage that stamped it
+  unsigned int pad;
+  unsigned long long ns[kStages];  // summed time from a stage's stamp to the next stamp
+  unsigned int n[kStages];
+  unsigned long long busy[kStages];  // summed time from a stage's stamp to its kernel's last CTA done
 };
+static_assert(kStageOffset + sizeof(StageClock) <= 256, "stage clock inside the control block");
 
+// Token tiles: an expert with more than 256 tokens in a call is cut into tiles of 256,
+// each its own unit of the FFN kernel; ntc bounds the tiles of any expert (counter stride).
 inline int token_tile_cap(size_t Tk) { return Tk > 256 ? static_cast<int>((Tk + 255) / 256) : 1; }
 
 // Device scratch for one layer call.  Every buffer is owned by the caller (one
@@ -68,8 +77,8 @@ struct WsLayout {
   size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert
   size_t done;        // int32 [ndone] [0] FFN work counter, [1] CTAs done gathering xp, then
                       //               [E*S*ntc] finished gate/up tiles per (expert, down split,
-                      //               token tile), then [E*m1*ntc] gate/up K slices stored per
-                      //               (expert, feature tile, token tile) when ks1 > 1
+                      //               token tile), then [E*m2*ntc] finished down units per
+                      //               (expert, row tile, token tile)
   size_t xp;          // elem  [rows, H] token rows in expert-major order (gathered by the FFN kernel)
   size_t perm;        // int32 [Tk]    perm[p] = flat slot f = t*k + j at position p
   size_t inv;         // int32 [Tk]    inv[f] = p
@@ -78,25 +87,21 @@ struct WsLayout {
   size_t logits;      // fp32  [T, E]  router logits of the gated launch (rounded to the storage dtype)
   size_t a2;          // elem  [rows, I] silu(x W1^T) * (x W3^T) in expert-major order
   size_t part;        // fp32  [S, Tk, H] split-K partials of the down projection
-  size_t gu;          // fp32  [ks1-1, rows, 2I] gate/up partials of the K slices before the last
   size_t total;
   int rows;           // padded row count of xp / a2
   int splits;         // S
-  int ks1;            // gate/up K slices
   int ntc;            // token-tile bound per expert
   int ndone;          // int32 counters in `done`
 };
 
-inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes, FfnPlan plan) {
+inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes, int splits) {
   WsLayout L{};
   const size_t Tk = static_cast<size_t>(T) * static_cast<size_t>(k);
   L.rows = static_cast<int>(align_up(Tk, 64) + 64);
-  L.splits = plan.splits;
-  L.ks1 = plan.ks1;
+  L.splits = splits;
   L.ntc = token_tile_cap(Tk);
-  const size_t m1 = (static_cast<size_t>(I) + 127) / 128;
-  L.ndone = static_cast<int>(2 + static_cast<size_t>(E) * plan.splits * L.ntc +
-                             (plan.ks1 > 1 ? static_cast<size_t>(E) * m1 * L.ntc : 0));
+  const size_t m2 = (static_cast<size_t>(H) + 255) / 256;
+  L.ndone = static_cast<int>(2 + static_cast<size_t>(E) * (splits + m2) * L.ntc);
   size_t o = 0;
   L.status = o;     o = align_up(o + sizeof(int32_t) * 64, kAlign);
   L.expert_off = o; o = align_up(o + sizeof(int32_t) * (E + 1), kAlign);
@@ -108,8 +113,7 @@ inline WsLayout make_ws_layout(int T, int E, int k, int H, int I, int elem_bytes
   L.logits = o;     o = align_up(o + sizeof(float) * static_cast<size_t>(T) * E, kAlign);
   L.xp = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * H, kAlign);
   L.a2 = o;         o = align_up(o + static_cast<size_t>(elem_bytes) * L.rows * I, kAlign);
-  L.part = o;       o = align_up(o + sizeof(float) * static_cast<size_t>(plan.splits) * Tk * H, kAlign);
-  L.gu = o;         o = align_up(o + sizeof(float) * static_cast<size_t>(plan.ks1 - 1) * L.rows * 2 * I, kAlign);
+  L.part = o;       o = align_up(o + sizeof(float) * static_cast<size_t>(splits) * Tk * H, kAlign);
   L.total = o;
   return L;
 }
@@ -138,44 +142,38 @@ inline EpArena make_ep_arena(int G, int C, int H, int elem_bytes) {
 }
 constexpr int kEpReturnFlags = 8;  // offset of the return flags in the flag block
 
-// Unit plan of the FFN kernel, chosen by simulating its dynamic unit queue on `num_sms`
-// SMs.  Gate/up K slices: when the touched experts give fewer gate/up units (256 weight
-// rows each) than SMs, every unit is cut into ks1 in {2, 4} K slices so that the first
-// wave fills the GPU.  Down split-K factor S: more splits make smaller down units (256 rows
-// x I/S), so the run ends with less idle time, but add fp32 partials (S x Tk x H x 4 B)
-// that the epilogue writes and the combine reads back.  The simulation hands units to the
+// Split-K factor of the down projection, chosen by simulating the FFN kernel's dynamic
+// unit queue on `num_sms` SMs.  More splits make smaller down units (256 rows x I/S), so
+// the run ends with less idle time, but add fp32 partials (S x rows x H x 4 B) that the
+// epilogue writes and the combine reads back.  The simulation hands units to the
 // earliest free SM in claim order (all gate/up units, then down units expert by expert,
-// split by split), each streaming its weights at 44 GB/s per SM, and a down unit starts no
-// earlier than the gate/up units that cover its K range (its token rows).  Cost =
+// split by split), each streaming its weights at 44 GB/s per SM, and a down unit starts
+// no earlier than the gate/up units that cover its K range (its token rows).  Cost =
 // simulated makespan + 2 x the partials' write+read time at 6.5 TB/s (the factor fitted
-// to graph-replay sweeps).  Measured optima it reproduces: Mixtral-8x7B T=256 -> S=2,
-// Mixtral-8x22B T=512 -> S=3.  Touched experts are estimated as min(E, Tk).
-inline FfnPlan choose_plan(int E, int H, int I, int Tk, int num_sms) {
+// to graph-replay sweeps).  `valid_tk` is the number of slots expected to hold a token
+// (default Tk): the expert side of an expert-parallel layer reserves G x C slots of
+// which about C are used.  Touched experts are estimated as min(E, valid_tk).  Measured
+// optima it reproduces: Mixtral-8x7B T=256 -> 2, Mixtral-8x22B T=512 -> 3, one
+// Mixtral-8x7B expert of an 8-rank layer (512 slots, ~64 used) -> 9.
+inline int choose_splits(int E, int H, int I, int Tk, int num_sms, int valid_tk = -1) {
   const double rate = 44e9, hbm = 6.5e12, part_factor = 2.0;
   const int kb2 = I / 64;
-  const int et = E < Tk ? E : (Tk > 0 ? Tk : 1);
+  const int vt = valid_tk >= 0 && valid_tk < Tk ? valid_tk : Tk;
+  const int et = E < vt ? E : (vt > 0 ? vt : 1);
   const int sms = num_sms > 0 ? num_sms : 1;
   const int m1 = (I + 127) / 128;
   const int m2 = (H + 255) / 256;
   const int smax = kb2 < 16 ? kb2 : 16;
-  FfnPlan plan;
-  plan.ks1 = 1;
-  while (static_cast<long long>(et) * m1 * plan.ks1 < sms && plan.ks1 < 4 && (H / 64) % (plan.ks1 * 2) == 0) {
-    plan.ks1 *= 2;
-  }
-  const int ks1 = plan.ks1;
   typedef std::priority_queue<double, std::vector<double>, std::greater<double>> Heap;
-  // phase 1 is the same for every S: simulate it once; a feature tile is ready when its
-  // last K slice is
+  // phase 1 is the same for every S: simulate it once
   Heap base;
   for (int i = 0; i < sms; ++i) base.push(0.0);
-  std::vector<double> done1(static_cast<size_t>(et) * m1, 0.0);
-  const double d1 = 256.0 * H * 2 / rate / ks1;
-  for (size_t u = 0; u < done1.size() * ks1; ++u) {
+  std::vector<double> done1(static_cast<size_t>(et) * m1);
+  const double d1 = 256.0 * H * 2 / rate;
+  for (size_t u = 0; u < done1.size(); ++u) {
     const double t = base.top();
     base.pop();
-    const size_t tile = u / ks1;
-    done1[tile] = done1[tile] > t + d1 ? done1[tile] : t + d1;
+    done1[u] = t + d1;
     base.push(t + d1);
   }
   int best = 1;
@@ -203,17 +201,13 @@ inline FfnPlan choose_plan(int E, int H, int I, int Tk, int num_sms) {
       make = q.top() > make ? q.top() : make;
       q.pop();
     }
-    const double cost = make + part_factor * 2.0 * s * static_cast<double>(Tk) * H * 4 / hbm;
+    const double cost = make + part_factor * 2.0 * s * static_cast<double>(vt) * H * 4 / hbm;
     if (cost < best_t * 0.999) {
       best_t = cost;
       best = s;
     }
   }
-  plan.splits = best;
-  return plan;
+  return best;
 }
-
-// Down split-K factor alone (the plan's S).
-inline int choose_splits(int E, int H, int I, int Tk, int num_sms) { return choose_plan(E, H, I, Tk, num_sms).splits; }
 
 }  // namespace smb

@@ -159,7 +159,6 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   int32_t* s_cnt = reinterpret_cast<int32_t*>(s_w + Tk); // [warps][E]
   int32_t* s_off = s_cnt + kRouteWarps * E;              // [E+1]
   __shared__ int s_bad;
-  __shared__ int s_ready;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -188,47 +187,6 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
       const int f = t * a.k + a.k_routed + q;
       s_ids[f] = Er + q;
       s_w[f] = a.shared_w != nullptr ? a.shared_w[t] : 1.0f;
-    }
-  } else if (a.ep_recv != nullptr) {
-    // expert side of the exchange: payload row f = s*C + i of source s belongs to the
-    // local expert whose run of the source's header counts holds i (k = 1, weight 1).
-    // Over peer memory the chunks are complete once every source has raised its flag to
-    // this call's epoch; if one does not within the wait budget, no row is taken.
-    const size_t row_bytes = static_cast<size_t>(a.H) * 2;
-    if (tid == 0) {
-      s_ready = 1;
-      if (a.link.p2p) {
-        const uint64_t tw = global_timer_ns();
-        s_ready = wait_flags_sys(a.link.wait_flags, a.link.nranks, a.link.ctrl[0] + 1) ? 1 : 0;
-        if (!s_ready) record_status(a.status, kDevTimeout);
-        if (cta == 0 && a.status != nullptr) {
-          DevTimers* tm = timers_of(a.status);
-          add_wait_time(&tm->recv_wait_ns, &tm->recv_waits, tw);
-        }
-      }
-    }
-    __syncthreads();
-    for (int f = tid; f < Tk; f += kRouteThreads) {
-      if (!s_ready) {
-        s_ids[f] = -1;
-        s_w[f] = 0.0f;
-        continue;
-      }
-      const int src = f / a.ep_C;
-      const int i = f - src * a.ep_C;
-      const int32_t* hdr = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(a.ep_recv) +
-                                                            static_cast<size_t>(src) * (a.ep_C + 1) * row_bytes);
-      int id = -1, acc = 0;
-      for (int e = 0; e < a.ep_Eloc; ++e) {
-        const int c = __ldcg(hdr + e);  // written by the source GPU while this grid waited
-        if (i < acc + c) {
-          id = e;
-          break;
-        }
-        acc += c;
-      }
-      s_ids[f] = id;
-      s_w[f] = 1.0f;
     }
   } else {
     // given routing [T, k_routed] (+ the shared slots, as above)
@@ -352,14 +310,8 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   // expert-parallel dispatch: token rows of this CTA's flat range into the exchange
   // layout, all threads on all rows, four independent 16-byte loads in flight per thread
   if (a.ep_send == nullptr) return;  // the FFN reads token rows through the permutation
-  const uint4* xsrc = reinterpret_cast<const uint4*>(a.ep_recv != nullptr ? a.ep_recv : a.x);
+  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
   const size_t row_bytes_out = static_cast<size_t>(vec_per_row) * 16;
-  // source row of token t: plain, or payload row t of the exchange layout
-  auto src_row = [&](int t) -> size_t {
-    if (a.ep_recv == nullptr) return static_cast<size_t>(t);
-    const int s = t / a.ep_C;
-    return static_cast<size_t>(s) * (a.ep_C + 1) + 1 + (t - s * a.ep_C);
-  };
   // destination row of flat slot f at expert-major position p: payload row
   // p - (first position of the destination's experts) of the destination's chunk
   auto dst_row = [&](int f, int p) -> uint4* {
@@ -375,7 +327,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
       const int i = base + j * kRouteThreads;
       if (i < nvec) {
         const int f = g0 + i / vec_per_row;
-        if (s_pos[f] >= 0) v[j] = __ldg(xsrc + src_row(f / a.k) * vec_per_row + (i % vec_per_row));
+        if (s_pos[f] >= 0) v[j] = __ldg(xsrc + static_cast<size_t>(f / a.k) * vec_per_row + (i % vec_per_row));
       }
     }
 #pragma unroll
@@ -394,16 +346,112 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     if (last_cta_of_grid(a.link.ctrl + 1, &s_last) && tid == 0) {
       const int epoch = a.link.ctrl[0] + 1;
       for (int d = 0; d < a.link.nranks; ++d) st_release_sys(a.link.flag[d], epoch);
+      stage_busy(a.clk, a.stage);
     }
   }
+}
+
+// Expert side of the exchange (one CTA): the received payload slots f = s*C + i through
+// the E_loc local experts, from the G x E_loc header counts alone.  Payload row i of
+// source s belongs to the expert whose run of s's counts holds i; positions are
+// expert-major with ascending f inside an expert (sources in order, then rows), so row
+// (s, i) of expert e sits at off[e] + (rows of e from sources before s) + (i - first row
+// of e in chunk s) - the order the generic permutation gives, in one pass.  Counts are
+// clamped to the chunk's C rows.  Over peer memory the chunks are complete once every
+// source has raised its flag to this call's epoch; if one does not within the wait
+// budget, no row is taken.
+__device__ __forceinline__ void route_receive(const RouteArgs& a, int32_t* sm) {
+  const int G = a.ep_G, C = a.ep_C, El = a.ep_Eloc;
+  const int Tk = a.T * a.k;  // G*C slots (k = 1)
+  int32_t* s_cnt = sm;                // [G*El] rows of (source, expert)
+  int32_t* s_base = s_cnt + G * El;   // [G*El] position of the first of them
+  int32_t* s_start = s_base + G * El; // [G*El] their first row inside the source's chunk
+  int32_t* s_off = s_start + G * El;  // [El+1]
+  __shared__ int s_ready;
+  const int tid = threadIdx.x;
+  const size_t row_bytes = static_cast<size_t>(a.H) * 2;
+  if (tid == 0) {
+    if (a.status != nullptr) a.status[0] = 0;
+    s_ready = 1;
+    if (a.link.p2p) {
+      const uint64_t tw = global_timer_ns();
+      s_ready = wait_flags_sys(a.link.wait_flags, a.link.nranks, a.link.ctrl[0] + 1) ? 1 : 0;
+      if (!s_ready) record_status(a.status, kDevTimeout);
+      if (a.status != nullptr) {
+        DevTimers* tm = timers_of(a.status);
+        add_wait_time(&tm->recv_wait_ns, &tm->recv_waits, tw);
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * El; i += kRouteThreads) {
+    const int src = i / El, e = i - (i / El) * El;
+    const int32_t* hdr = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(a.ep_recv) +
+                                                          static_cast<size_t>(src) * (C + 1) * row_bytes);
+    s_cnt[i] = s_ready ? __ldcg(hdr + e) : 0;  // written by the source GPU while this grid waited
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int src = 0; src < G; ++src) {
+      int run = 0;
+      for (int e = 0; e < El; ++e) {
+        int c = s_cnt[src * El + e];
+        c = max(0, min(c, C - run));
+        s_cnt[src * El + e] = c;
+        s_start[src * El + e] = run;
+        run += c;
+      }
+    }
+    int pos = 0;
+    for (int e = 0; e < El; ++e) {
+      s_off[e] = pos;
+      for (int src = 0; src < G; ++src) {
+        s_base[src * El + e] = pos;
+        pos += s_cnt[src * El + e];
+      }
+    }
+    s_off[El] = pos;
+  }
+  __syncthreads();
+  for (int e = tid; e <= El; e += kRouteThreads) a.expert_off[e] = s_off[e];
+  if (a.done != nullptr) {
+    for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
+  }
+  for (int f = tid; f < Tk; f += kRouteThreads) {
+    const int src = f / C, i = f - (f / C) * C;
+    int id = -1, p = -1;
+    for (int e = 0; e < El; ++e) {
+      const int q = src * El + e;
+      if (i >= s_start[q] && i < s_start[q] + s_cnt[q]) {
+        id = e;
+        p = s_base[q] + (i - s_start[q]);
+        break;
+      }
+    }
+    if (p >= 0) a.perm[p] = f;
+    a.inv[f] = p;
+    a.ws_w[f] = 1.0f;
+    a.ws_ids[f] = id;
+  }
+  __syncthreads();
+  if (tid == 0) stage_busy(a.clk, a.stage);
 }
 
 template <typename TL>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a, int vec_per_row) {
   extern __shared__ int32_t sm[];
   pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && threadIdx.x == 0) stage_mark(a.clk, a.stage);
   pdl_launch_dependents();
+  if (a.ep_recv != nullptr && a.ep_send == nullptr) {
+    route_receive(a, sm);
+    return;
+  }
   route_body<TL>(a, vec_per_row, static_cast<int>(blockIdx.x), sm);
+  if (gridDim.x == 1) {
+    __syncthreads();
+    if (threadIdx.x == 0) stage_busy(a.clk, a.stage);
+  }
 }
 
 // ---------------------------------------------------------------------------- gate
@@ -435,6 +483,7 @@ __global__ void __launch_bounds__(kRouteThreads) gate_route_kernel(const RouteAr
   __shared__ float s_red[kRouteWarps][kGateTok * kGateExp];
   __shared__ int s_last;
   pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && g.route) stage_mark(a.clk, a.stage);
   pdl_launch_dependents();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;

@@ -86,7 +86,7 @@ class CudaBackend:
                 num_local: int) -> torch.Tensor:
         """Expert output of every payload row of the received chunks, [G*C, H]."""
         from . import _native, ops
-        nbytes = ops.workspace_bytes(G * C, num_local, 1, self.H, self.I, self.dtype)
+        nbytes = ops.ep_workspace_bytes(G, C, num_local, self.H, self.I, self.dtype)
         ws = self._buf(("ws_exp", G, C), nbytes=nbytes)
         out = self._buf(("y", G, C), shape=(G * C, self.H), dtype=self.dtype)
         _native.call("smb_moe_ep_experts", recv.data_ptr(), G, C, pool.data_ptr(), pool.shape[0], pages.data_ptr(),
@@ -186,7 +186,7 @@ class P2PBackend(CudaBackend):
         T = x.shape[0]
         nb = ops.workspace_bytes(max(T, 1), self.E, self.k, self.H, self.I, self.dtype)
         ws = self._buf(("ws_src", T), nbytes=nb)
-        nbe = ops.workspace_bytes(G * C, num_local, 1, self.H, self.I, self.dtype)
+        nbe = ops.ep_workspace_bytes(G, C, num_local, self.H, self.I, self.dtype)
         wse = self._buf(("ws_exp", G, C), nbytes=nbe)
         out = self._buf(("out", T), shape=(T, self.H), dtype=self.dtype)
         st = self._stream()
@@ -287,7 +287,13 @@ class ExpertParallelMoE:
             if key[0] in ("ws_exp", "ws_src"):
                 t = ops.read_timers(buf, reset)
                 for name, v in t.items():
-                    out[name] = out.get(name, 0) + v
+                    if not isinstance(v, dict):
+                        out[name] = out.get(name, 0) + v
+        if self.transport is not None:
+            # over peer memory every kernel of a call stamps the stage clock of this rank's arena
+            t = ops.read_timers_at(self.transport.own, 256, self.device, reset)
+            out["stage_ns"], out["stage_calls"] = t["stage_ns"], t["stage_calls"]
+            out["stage_busy_ns"] = t["stage_busy_ns"]
         return out
 
     def status(self) -> int:

@@ -105,8 +105,13 @@ def splits(E: int, H: int, I: int, Tk: int) -> int:
     return _native.call("smb_moe_splits", E, H, I, Tk)
 
 
-def gate_up_slices(E: int, H: int, I: int, Tk: int) -> int:
-    return _native.call("smb_moe_gate_up_slices", E, H, I, Tk)
+def ep_workspace_bytes(G: int, C: int, E_loc: int, H: int, I: int, dtype: torch.dtype) -> int:
+    """Workspace of the expert side of a G-rank exchange with C slots per pair
+    (``smb_moe_ep_workspace_bytes``)."""
+    n = _native.load().smb_moe_ep_workspace_bytes(G, C, E_loc, H, I, storage_code(dtype))
+    if n == 0:
+        raise NotImplementedError(f"unsupported expert-parallel sizes G={G} C={C} E_loc={E_loc} H={H} I={I}")
+    return int(n)
 
 
 def pool_geometry(pool: torch.Tensor, H: int):
@@ -122,12 +127,18 @@ def pool_geometry(pool: torch.Tensor, H: int):
 def read_timers(ws: torch.Tensor, reset: bool = False) -> dict:
     """Device-side kernel timers accumulated in workspace ``ws`` (``smb_moe_read_timers``):
     ``ffn_ns`` / ``ffn_launches`` (FFN kernel launches, first CTA past its wait on the
-    router to the last CTA done) and the flag-wait times of the expert-parallel exchange.
-    Synchronises the current stream; ``reset`` then zeroes them, stream-ordered."""
+    router to the last CTA done), the flag-wait times of the expert-parallel exchange and
+    the per-stage times of the calls (``stage_ns`` / ``stage_calls``).  Synchronises the
+    current stream; ``reset`` then zeroes them, stream-ordered."""
+    return read_timers_at(ws.data_ptr(), ws.numel(), ws.device, reset)
+
+
+def read_timers_at(ptr: int, nbytes: int, device, reset: bool = False) -> dict:
+    """``read_timers`` on a raw control block (a workspace, or an exchange arena)."""
     import ctypes
     t = _native.Timers()
-    _native.call("smb_moe_read_timers", ws.data_ptr(), ws.numel(), int(bool(reset)), ctypes.byref(t),
-                 _stream_ptr(ws.device))
+    _native.call("smb_moe_read_timers", ptr, nbytes, int(bool(reset)), ctypes.byref(t),
+                 _stream_ptr(torch.device(device)))
     return t.as_dict()
 
 
@@ -393,17 +404,15 @@ class StagedLayer:
 
         rows = up_to(Tk, 64) + 64
         S = splits(E, H, I, Tk)
-        K1 = gate_up_slices(E, H, I, Tk)
         ntc = -(-Tk // 256) if Tk > 256 else 1
-        m1 = -(-I // 128)
-        ndone = 2 + E * S * ntc + (E * m1 * ntc if K1 > 1 else 0)
+        ndone = 2 + E * (S + -(-H // 256)) * ntc
         o = 0
         off = {}
         # mirrors ae_b200/csrc/layout.h::make_ws_layout (checked against its total below)
         for name, nb in (("status", 4 * 64), ("expert_off", 4 * (E + 1)), ("done", 4 * ndone),
                          ("perm", 4 * Tk), ("inv", 4 * Tk), ("w", 4 * Tk), ("ids", 4 * Tk),
                          ("logits", 4 * self.T * E), ("xp", 2 * rows * H), ("a2", 2 * rows * I),
-                         ("part", 4 * S * Tk * H), ("gu", 4 * (K1 - 1) * rows * 2 * I)):
+                         ("part", 4 * S * Tk * H)):
             off[name] = (o, nb)
             o = up(o + nb)
         if o != self.nbytes:

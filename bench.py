@@ -238,6 +238,19 @@ def algorithmic(cfg, touched: int, T: int | None = None):
     return ffn, layer, flops
 
 
+def stage_means(tm: dict, busy: bool = False) -> dict:
+    """Mean µs per call of each stage of the chain from the library's stage clock (a stage
+    runs from its first kernel block passing its wait to the next stage's; with ``busy``,
+    the part until the stage's kernel finished)."""
+    out = {}
+    key = "stage_busy_ns" if busy else "stage_ns"
+    for name, ns in tm.get(key, {}).items():
+        n = tm["stage_calls"][name]
+        if n:
+            out[name] = round(ns / n / 1e3, 2)
+    return out
+
+
 def touched_experts(logits, k: int, renormalize: bool = True) -> int:
     """Experts that at least one token picks, from the library's own routing of the logits."""
     from ae_b200 import ops
@@ -350,6 +363,7 @@ def run_ours(args, cfg, rank, world, dev):
     if tm["ffn_launches"] != args.steps:
         raise RuntimeError(f"FFN timer saw {tm['ffn_launches']} launches in {args.steps} timed steps")
     ffn_s = tm["ffn_ns"] / tm["ffn_launches"] * 1e-9
+    stages = {"stage_us": stage_means(tm), "kernel_busy_us": stage_means(tm, busy=True)}
     if not torch.isfinite(out.float()).all():
         raise RuntimeError("non-finite layer output")
     timed_out = out.clone()
@@ -549,6 +563,7 @@ def run_ours(args, cfg, rank, world, dev):
                            "frac_hbm": round(layer_bytes / step_s / 1e9 / hbm_peak, 4),
                            "tflops": round(flops / step_s / 1e12, 2),
                            "frac_tensor": round(flops / step_s / 1e12 / tc_peak, 4)},
+        "stages_us": stages,
         "kernels_us": {n: round(u, 2) for n, u in kern_us.items()},
         "kernels_timing": "CUDA events between eager launches of the three kernels (staged pass after the timed "
                           "region)",
@@ -780,6 +795,9 @@ def bench_verify_step(dev, stream, hbm_peak, steps: int = 5):
     return out
 
 
+EP_STAGES = ("route", "recv_route", "ffn", "final_combine")
+
+
 def ep_time(moe, x, logits, dev, stream, steps, soak=0.0):
     """Graph-replay time of ``steps`` expert-parallel layer calls (max over ranks) with the
     ranks' device timers over exactly those calls.  Returns (seconds, timers per rank as a
@@ -814,10 +832,14 @@ def ep_time(moe, x, logits, dev, stream, steps, soak=0.0):
     torch.cuda.synchronize(dev)
     dist.barrier()
     tm = moe.timers()
+    st = stage_means(tm)
+    sb = stage_means(tm, busy=True)
     mine = torch.tensor([elapsed, tm.get("ffn_ns", 0) / max(1, tm.get("ffn_launches", 0)) * 1e-3,
                          tm.get("recv_wait_ns", 0) / max(1, tm.get("recv_waits", 0)) * 1e-3,
                          tm.get("combine_wait_ns", 0) / max(1, tm.get("combine_waits", 0)) * 1e-3,
-                         tm.get("ffn_launches", 0), tm.get("recv_waits", 0)], device=dev, dtype=torch.float64)
+                         tm.get("ffn_launches", 0), tm.get("recv_waits", 0)] +
+                        [st.get(n, 0.0) for n in EP_STAGES] + [sb.get(n, 0.0) for n in EP_STAGES],
+                        device=dev, dtype=torch.float64)
     every = [torch.empty_like(mine) for _ in range(dist.get_world_size())]
     dist.all_gather(every, mine)
     every = torch.stack(every)
@@ -989,16 +1011,20 @@ def run_ep(args, cfg, rank, world, dev):
                 f"(Wr std {cfg.router_std:.4g})",
         "config": config_of(cfg, world),
         "roofline": {"bound": "hbm", "kernel": "local experts on the received rows (smb_moe_ep_experts: "
-                                                "route_kernel + ffn_gemm_kernel + combine_kernel), slowest rank",
+                                                "route_kernel + ffn_gemm_kernel), slowest rank",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None},
         "per_rank_device_timers_us": {
             "ffn": [round(float(v), 2) for v in pr[:, 1]],
             "recv_flag_wait": [round(float(v), 2) for v in pr[:, 2]],
             "return_flag_wait": [round(float(v), 2) for v in pr[:, 3]],
+            "stages": {n: [round(float(v), 2) for v in pr[:, 6 + i]] for i, n in enumerate(EP_STAGES)},
+            "stage_kernel_busy": {n: [round(float(v), 2) for v in pr[:, 6 + len(EP_STAGES) + i]]
+                                  for i, n in enumerate(EP_STAGES)},
             "timing": "device timers over the timed replays (means per call): FFN kernel (first CTA past its "
                       "wait to last CTA done), expert-side wait for the sources' rows, source-side wait for "
-                      "the returned rows"},
+                      "the returned rows; stages of the chain from the arena's stage clock (dispatch, receive "
+                      "routing, FFN with the returned rows written, final combine up to the next call's dispatch)"},
         "parity": parity,
         "cpu_baseline": None,
         "e2e": {"value": round(cfg.T * args.steps / e2e_el, 2), "unit": UNIT,
@@ -1006,7 +1032,7 @@ def run_ep(args, cfg, rank, world, dev):
                 "d2h_bytes_per_step": world * x.numel() * x.element_size(),
                 "api": f"ae_b200.ep.ExpertParallelMoE.forward (transport={args.ep_transport})"},
         f"{other}_transport_us_per_layer": round(t2 / args.steps * 1e6, 2),
-        "gpu_launches": (3 if args.ep_transport == "p2p" else 5) * args.steps,
+        "gpu_launches": 4 * args.steps,
         "clocks": clocks,
         "c5_expert_parallel": c5,
     }

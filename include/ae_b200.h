@@ -82,11 +82,6 @@ SMB_API size_t smb_moe_workspace_bytes(int T, int E, int k, int H, int I, int dt
  * device. */
 SMB_API int smb_moe_splits(int E, int H, int I, int Tk);
 
-/* K slices the gate/up projection is cut into for these sizes on the current device (1, or
- * 2 / 4 when the touched experts give fewer gate/up units than SMs, e.g. one expert per
- * rank of an expert-parallel layer; the slices before the last store fp32 partials in the
- * workspace that the last slice adds). */
-SMB_API int smb_moe_gate_up_slices(int E, int H, int I, int Tk);
 
 /* Router: softmax over E in fp32, top-k (ties to the lower expert index), optional
  * renormalisation; then the expert-major permutation (positions in the workspace).  Replaces select_experts (FusedMoE.py:174-185) + moe_align_block_size
@@ -156,10 +151,17 @@ SMB_API int smb_moe_ep_dispatch(const void* router_logits, int logits_dtype, con
                                 float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes,
                                 smb_stream_t stream);
 
+/* Workspace of the expert side of a G-rank exchange with C slots per (source, rank)
+ * pair: the layout of smb_moe_workspace_bytes(G*C, E_loc, 1, H, I, dtype) with the
+ * down split-K factor chosen for the ~C slots that hold a token (a source sends each rank
+ * C/G rows on average), not for all G*C. */
+SMB_API size_t smb_moe_ep_workspace_bytes(int G, int C, int E_loc, int H, int I, int dtype);
+
 /* Expert side: the received chunks recv [G][C+1][H] through this rank's E_loc experts
  * (pool / page_of_expert hold the local pages); out_rows [G][C][H] gets each payload
- * row's expert output (zero past a chunk's counts).  ws is sized for T = G*C, E = E_loc,
- * k = 1 (smb_moe_workspace_bytes(G*C, E_loc, 1, H, I, dtype)). */
+ * row's expert output (rows past a chunk's counts are not written).  The FFN kernel
+ * writes the rows itself (the down units that complete an output tile sum its split-K
+ * partials).  ws is sized by smb_moe_ep_workspace_bytes(G, C, E_loc, H, I, dtype). */
 SMB_API int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t num_pages,
                                const int64_t* page_of_expert, int dtype, int E_loc, int H, int I, void* out_rows,
                                void* ws, size_t ws_bytes, smb_stream_t stream);
@@ -183,6 +185,8 @@ SMB_API int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, in
  *   experts: waits (bounded) for the G flags, runs the local experts, writes each row's
  *     output into its source's arena and raises a flag there;
  *   combine: waits (bounded) for the G return flags, weighted sum into out [T,H].
+ * The experts call is two kernels (receive routing from the header counts, then the FFN,
+ * whose last CTA raises the return flags), so a layer call is four kernels per rank.
  * Flags carry an epoch kept in the arena (the count of finished calls), so calls can be
  * replayed from a CUDA graph.  A wait that runs out (2 s) records SMB_ERR_DEVICE_TIMEOUT in
  * the workspace status (smb_moe_read_status) and the call continues without the missing
@@ -324,7 +328,17 @@ SMB_API int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, i
  *   recv_wait_ns / recv_waits: expert side of the peer-memory exchange, time the receive
  *     router waited for the sources' flags;
  *   combine_wait_ns / combine_waits: source side, time the final combine waited for the
- *     returned rows.
+ *     returned rows;
+ *   stage_ns[i] / stage_calls[i]: per stage of a layer call, from the stage's first kernel
+ *     block passing its wait on the previous kernel to the next stage's; stages 0 routing
+ *     (expert-parallel: dispatch), 1 expert-side receive routing, 2 FFN (expert-parallel:
+ *     with the returned rows written), 3 combine, 4 source-side final combine; the last stage
+ *     of a call ends when the next call starts; stage_busy_ns[i]: the part of it until the
+ *     stage's kernel finished (recorded by its last CTA where the kernel keeps a CTA
+ *     ticket: the gated or single-CTA routing, the dispatch and receive routing over peer
+ *     memory, the FFN, the final combine over peer memory).  Over peer memory the whole chain keeps
+ *     its stage clock in the rank's exchange arena: pass the arena (its own, at least 256
+ *     bytes) as `ws` to read it.
  * Reads synchronously on `stream`; reset != 0 then zeroes the timers (stream-ordered). */
 typedef struct smb_timers {
   uint64_t ffn_ns;
@@ -334,6 +348,10 @@ typedef struct smb_timers {
   uint32_t recv_waits;
   uint32_t combine_waits;
   uint32_t reserved;
+  uint64_t stage_ns[5];
+  uint32_t stage_calls[5];
+  uint32_t reserved2;
+  uint64_t stage_busy_ns[5];
 } smb_timers_t;
 SMB_API int smb_moe_read_timers(const void* ws, size_t ws_bytes, int reset, smb_timers_t* out, smb_stream_t stream);
 

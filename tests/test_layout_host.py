@@ -20,20 +20,16 @@ int main() {
     {"c2_t256", 8, 4096, 14336, 512}, {"c5_t512", 8, 6144, 16384, 1024},
     {"c2_t16", 8, 4096, 14336, 32}, {"c3", 60, 2048, 1408, 512}};
   for (auto& c : cs) std::printf("split %s %d\n", c.n, smb::choose_splits(c.E, c.H, c.I, c.Tk, sms));
-  // gate/up K slices: one Mixtral expert on each of 8 ranks (512 exchange rows), two on
-  // each of 4, and the single-GPU verify batch
-  std::printf("slices ep8 %d\n", smb::choose_plan(1, 4096, 14336, 512, sms).ks1);
-  std::printf("slices ep4 %d\n", smb::choose_plan(2, 4096, 14336, 512, sms).ks1);
-  std::printf("slices c2_t256 %d\n", smb::choose_plan(8, 4096, 14336, 512, sms).ks1);
-  const smb::WsLayout ep8 = smb::make_ws_layout(512, 1, 1, 4096, 14336, 2, smb::choose_plan(1, 4096, 14336, 512, sms));
-  std::printf("ep8_gu_bytes %zu\n", ep8.total - ep8.gu);
-  std::printf("ep8_ndone %d\n", ep8.ndone);
-  const smb::WsLayout pf = smb::make_ws_layout(2048, 8, 2, 4096, 14336, 2, smb::choose_plan(8, 4096, 14336, 4096, sms));
+  // the expert side of an expert-parallel layer: G x C slots, about C used
+  std::printf("split ep8 %d\n", smb::choose_splits(1, 4096, 14336, 512, sms, 64));
+  std::printf("split ep8_unhinted %d\n", smb::choose_splits(1, 4096, 14336, 512, sms));
+  const smb::WsLayout pf = smb::make_ws_layout(2048, 8, 2, 4096, 14336, 2, smb::choose_splits(8, 4096, 14336, 4096, sms));
   std::printf("prefill_ntc %d\n", pf.ntc);
+  std::printf("prefill_ndone %d\n", pf.ndone);
   int first_over = -1;
   for (int T = 1; T <= 1024 && first_over < 0; ++T) {
-    const smb::FfnPlan p = smb::choose_plan(8, 4096, 14336, 2 * T, sms);
-    if (smb::make_ws_layout(T, 8, 2, 4096, 14336, 2, p).total > (64u << 20)) first_over = T;
+    const int s = smb::choose_splits(8, 4096, 14336, 2 * T, sms);
+    if (smb::make_ws_layout(T, 8, 2, 4096, 14336, 2, s).total > (64u << 20)) first_over = T;
   }
   std::printf("noalloc_first_over %d\n", first_over);
   const smb::EpArena a = smb::make_ep_arena(8, 64, 4096, 2);
@@ -59,7 +55,7 @@ def planning():
     res = {}
     for line in out.splitlines():
         parts = line.split()
-        res[" ".join(parts[:-1]) if parts[0] in ("split", "slices") else parts[0]] = \
+        res[" ".join(parts[:-1]) if parts[0] == "split" else parts[0]] = \
             parts[1:] if parts[0] == "arena" else int(parts[-1])
     return res
 
@@ -72,16 +68,16 @@ def test_split_k_choices_match_measured_optima(planning):
     assert planning["split c2_t16"] >= 8
 
 
-def test_gate_up_slices_only_when_units_underfill_the_gpu(planning):
-    # one Mixtral-8x7B expert gives 112 gate/up units for 148 SMs: two K slices (224 units)
-    assert planning["slices ep8"] == 2
-    assert planning["slices ep4"] == 1
-    assert planning["slices c2_t256"] == 1
-    # the first slice's fp32 gate/up partials: [rows = 512 + 64, 2 * 14336] floats
-    assert planning["ep8_gu_bytes"] == 576 * 2 * 14336 * 4
-    # counters: 2 + E*S*ntc + E*m1*ntc with ntc = 2 token tiles of 256 rows bound
-    assert planning["ep8_ndone"] >= 2 + 112 * 2
+def test_expert_side_split_uses_the_expected_rows(planning):
+    # one Mixtral-8x7B expert on each of 8 ranks: 512 exchange slots of which ~64 are
+    # used; graph-replay A/B on B200 (S in 3, 5, 7, 9): 9 best (FFN 77 us vs 87 us at S=5,
+    # the choice when the partials of all 512 slots are priced)
+    assert planning["split ep8"] == 9
+    assert planning["split ep8_unhinted"] == 5
+    # prefill-sized call: 512 tokens per expert -> up to 16 token tiles of 256 per expert,
+    # counters 2 + E * (S + H/256) * 16
     assert planning["prefill_ntc"] == 16
+    assert planning["prefill_ndone"] >= 2 + 8 * (1 + 16) * 16
 
 
 def test_noalloc_limit_statement(planning):
