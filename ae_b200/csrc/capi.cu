@@ -382,6 +382,19 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
+// Prefill-sized calls (at least 256 routed slots per expert on average, both phases, no
+// streamed pages or exchange output) go to the CTA-pair kernels: there the tensor pipe,
+// not HBM, bounds the layer.  SMB_PAIR=0 / 1 forces the choice (experiments).
+bool use_pair_path(int Tk, int E, int phases, bool special) {
+  if (phases != 3 || special) return false;
+  static const int forced = [] {
+    const char* v = std::getenv("SMB_PAIR");
+    return v == nullptr ? -1 : (v[0] == '1' ? 1 : 0);
+  }();
+  if (forced >= 0) return forced == 1;
+  return static_cast<long long>(Tk) >= 256LL * E;
+}
+
 // phase bit 1: gate/up GEMM (+SiLU*mul), bit 2: down GEMM (split-K partials); both bits
 // run both phases in one persistent launch.
 int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
@@ -447,6 +460,14 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
     // standalone call: the router zeroed the counters for the first FFN launch only
     cudaError_t err = cudaMemsetAsync(args.sched, 0, sizeof(int) * static_cast<size_t>(L.ndone), stream);
     if (err != cudaSuccess) return cuda_fail(err);
+  }
+  if (use_pair_path(T * k, E, phases, page_ready != nullptr || out_link != nullptr)) {
+    // prefill-sized: gate/up then down on CTA pairs (2-SM MMA), all pairs resident
+    const int pairs = ffn_pair_capacity(bf16);
+    if (pairs < 1) return cuda_fail(cudaErrorLaunchOutOfResources);
+    cudaError_t err = launch_ffn_pair(bf16, 1, pairs, stream, pdl_enabled(), w13, txp, args);
+    if (err == cudaSuccess) err = launch_ffn_pair(bf16, 2, pairs, stream, pdl_enabled(), w2, ta2, args);
+    return err == cudaSuccess ? SMB_OK : cuda_fail(err);
   }
   cudaError_t err = launch_ffn_gemm(bf16, di.sms, stream, pdl_enabled(), w13, w2, txp, ta2, args);
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);

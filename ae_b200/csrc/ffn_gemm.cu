@@ -650,8 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* stg = dyn_smem + (kDynSmem - kEpiStage) + sub * 2048;
       for (int c0 = 0; c0 < nlen; c0 += 16) {
         float va[16], vb[16];
-        tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
-        tmem_ld16(lane_base + acc1_off + static_cast<uint32_t>(c0), vb);
+        tmem_ld16x2(lane_base + static_cast<uint32_t>(c0), lane_base + acc1_off + static_cast<uint32_t>(c0), va, vb);
         const int nt = min(16, nlen - c0);
         if (un.phase == 1) {
           T* st = reinterpret_cast<T*>(stg);

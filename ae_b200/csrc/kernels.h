@@ -79,6 +79,13 @@ struct FfnArgs {
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
                             const CUtensorMap& w2, const CUtensorMap& xp, const CUtensorMap& a2, const FfnArgs& args);
 
+// Prefill-sized calls on CTA pairs (ffn_pair.cu): phase 1 = gate/up with SiLU*mul into a2
+// (w = the [P*3I, H] weight map, tok = xp), phase 2 = down split-K partials (w = the
+// [P*3H, I] map, tok = a2).  `pairs` pairs; ffn_pair_capacity = pairs resident at once.
+cudaError_t launch_ffn_pair(bool bf16, int phase, int pairs, cudaStream_t stream, bool pdl, const CUtensorMap& w,
+                            const CUtensorMap& tok, const FfnArgs& args);
+int ffn_pair_capacity(bool bf16);
+
 struct RouteArgs {
   const void* logits;      // [T, E] or nullptr (routing given)
   int logits_dtype;        // SMB_DTYPE_*

@@ -145,3 +145,31 @@ def test_device_timers_count_the_calls():
     ffn_stage = tm["stage_ns"]["ffn"] / 4
     ffn_kernel = tm["ffn_ns"] / 4
     assert ffn_kernel <= ffn_stage * 1.05 + 2000, (ffn_kernel, ffn_stage)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,E,k,H,I", [
+    (1024, 8, 2, 256, 128),    # pair tiles wider than I and H (rows past them never stored)
+    (1200, 6, 2, 512, 384),    # partial last token tiles of 256 (N a multiple of 32 < 256)
+])
+def test_cta_pair_path_vs_oracle(dtype, T, E, k, H, I):
+    """Prefill-sized calls (>= 256 routed slots per expert) run on CTA pairs with the 2-SM
+    MMA; checked against the fp32 oracle like the verify path."""
+    from ae_b200 import ops
+    dev = torch.device("cuda", 0)
+    assert T * k >= 256 * E
+    g = torch.Generator(device=dev)
+    g.manual_seed(T + H)
+    pool = (torch.randn(E + 2, 3 * I * H, generator=g, device=dev) * 0.05).to(dtype)
+    x = torch.randn(T, H, generator=g, device=dev).to(dtype)
+    logits = torch.randn(T, E, generator=g, device=dev).to(dtype)
+    pages = torch.randperm(E + 2, generator=g, device=dev)[:E].to(torch.int64)
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    out = ops.moe_forward(x, logits, pool, pages, k, True, topk_ids=ids)
+    torch.cuda.synchronize()
+    rw, rids = mo.select_experts(logits.cpu(), k, True)
+    assert (ids.cpu().numpy() == rids).all()
+    ref = mo.stack_fused_moe(x.cpu(), pool.cpu(), pages.cpu(), rw, rids, rounding="fp32").float()
+    max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+    print(f"PARITY pair path {dtype} T={T} E={E} H={H} I={I}: max_abs={max_abs:.4e} rel_l2={rel:.4e}")
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (max_abs, rel)
