@@ -1104,6 +1104,58 @@ def run_ep_rank(args, cfg, dev):
     emit({"ep_rank_emulation": {"workload": cfg.name, "ranks": G, "experts_per_rank": E_loc, **res}})
 
 
+def run_power_probe(args, cfg, dev):
+    """Diagnostic (``--power-probe``, no metric line): layer time against the SM clock.  One
+    graph of a layer call is replayed in blocks of 40: once after a 2 s idle gap, then back
+    to back for ``--probe-seconds``, then once more after a 3 s idle gap; each block reports
+    its µs per layer, the FFN kernel's device timer and the SM clock / throttle reasons
+    sampled during it."""
+    from ae_b200 import configs, ops
+    pool = configs.make_pool(cfg, dev, seed=0)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=0)
+    out = torch.empty_like(x)
+
+    def step():
+        ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out)
+
+    for _ in range(5):
+        step()
+    g, cs = graph_of(step, dev, with_stream=True)
+    ws = ops.Workspace.lookup(dev, cs)
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    blocks = []
+
+    def block(tag, n=40):
+        ops.read_timers(ws, reset=True)
+        t0 = time.time()
+        el = timed_steps(g.replay, n, stream)
+        tm = ops.read_timers(ws)
+        t1 = time.time()
+        c = sampler.summary(t0 - 0.15, t1 + 0.15)
+        blocks.append({"tag": tag, "us_per_layer": round(el / n * 1e6, 2),
+                       "ffn_us": round(tm["ffn_ns"] / max(1, tm["ffn_launches"]) / 1e3, 2),
+                       "sm_mhz": c["sm_mhz"], "reasons": c["reasons"]})
+
+    time.sleep(2.0)
+    block("after_idle_2s")
+    end = time.time() + args.probe_seconds
+    while time.time() < end:
+        block("sustained")
+    time.sleep(3.0)
+    block("after_idle_3s")
+    sampler.stop()
+    hot = [b for b in blocks if b["tag"] == "sustained"]
+    hot = hot[len(hot) // 2:]  # the settled half
+    emit({"power_probe": {"workload": cfg.name, "blocks_first_last": blocks[:2] + blocks[-2:],
+                          "sustained_median_us": statistics.median(b["us_per_layer"] for b in hot),
+                          "sustained_median_ffn_us": statistics.median(b["ffn_us"] for b in hot),
+                          "sustained_median_sm_mhz": statistics.median(b["sm_mhz"] or 0 for b in hot),
+                          "blocks": len(blocks)}})
+
+
 _JSON_OUT = None
 
 
@@ -1143,6 +1195,9 @@ def main():
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-alls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
+    ap.add_argument("--power-probe", action="store_true",
+                    help="diagnostic: layer time against the SM clock over a sustained run (no metric line)")
+    ap.add_argument("--probe-seconds", type=float, default=8.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1164,6 +1219,9 @@ def main():
     torch.cuda.set_device(dev)
     if args.ep_rank > 0:
         run_ep_rank(args, cfg, dev)
+        return
+    if args.power_probe:
+        run_power_probe(args, cfg, dev)
         return
     if world > 1:
         import torch.distributed as dist
