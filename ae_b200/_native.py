@@ -104,7 +104,8 @@ def load(path: str | None = None):
     with _lock:
         if _lib is not None:
             return _lib
-        p = path or LIB_PATH
+        # SMB_LIB: load another build of the same ABI (side-by-side comparisons)
+        p = path or os.environ.get("SMB_LIB") or LIB_PATH
         if not os.path.exists(p):
             raise RuntimeError(
                 f"ae_b200 CUDA library not found at {p}; build it with `python -m ae_b200.build`")

@@ -15,21 +15,25 @@
 // own 256 weight rows (gate and up of 128 features, or two 128-row blocks of w2) and only
 // half of the token tile: 48 KB per 64-wide K step for 8.4 MFLOP per SM, 25 % fewer bytes
 // per flop.  Two launches: gate/up (phase 1, SiLU*mul in the epilogue, activations in
-// storage dtype) then down (phase 2, split-K fp32 partials for the combine kernel).
+// storage dtype) then down (phase 2, split-K fp32 partials for the combine kernel; 32 KB
+// per K step for 4.2 MFLOP per SM, double-buffered accumulators).
 //
 // Per pair and unit (CTA rank r = 0 leader, 1 peer):
 //   phase 1: features [f0 + 128 r, +128) of w1 (gate) and w3 (up), tokens [n0, n0 + nb):
 //     accumulators gate [128 lanes x nb] at TMEM column 0 and up at column 256 in each
 //     CTA; lane l of CTA r holds feature f0 + 128 r + l, so SiLU*mul is local;
-//   phase 2: rows [h0 + 128 r, +128) and [h0 + 256 + 128 r, +128) of w2 over the split's K
-//     range: two accumulators, rows h0 + 128 r + l and h0 + 256 + 128 r + l.
-// Shared memory per stage and CTA: two 128-row weight boxes and nb/2 token rows (two
+//   phase 2: rows [h0 + 128 r, +128) of w2 over the split's K range: one accumulator per
+//     unit (row h0 + 128 r + l), two TMEM buffers, so the next unit's MMAs run while the
+//     epilogue drains the last; 256-row units also make twice as many units as 512-row
+//     ones, which the down launch needs to spread over the pairs in small waves (with
+//     512-row units 24 % of the SM time sat in the last partial wave).
+// Shared memory per stage and CTA: the unit's 128-row weight boxes and nb/2 token rows (two
 // 64-row boxes), all by TMA; both CTAs' bytes complete on the leader's full barrier, the
 // leader's MMA thread commits to both CTAs' empty barriers and TMEM-full barriers, and
 // both epilogues release the accumulators on the leader's TMEM-empty barrier.
 // Units are spread over the pairs statically (unit = pair + i * pairs), so both CTAs of
-// a pair walk the same list without talking.  The TMEM accumulators are single-buffered
-// (512 columns for two N = 256 accumulators); the epilogue of a unit is ~2-4 % of its MMA.
+// a pair walk the same list without talking.  The gate/up accumulators are single-
+// buffered (512 columns for two N = 256 accumulators).
 //
 // Every wait is bounded; after a failed wait the CTA stops, waits a bounded time for its
 // copies in flight, meets its peer and frees its TMEM.
@@ -45,11 +49,24 @@ namespace {
 constexpr int kPThreads = 192;                // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
 constexpr int kPBK = 64;
 constexpr int kPBox = 128 * kPBK * 2;         // 16 KB: 128 rows x 64 K
-constexpr int kPStageBytes = 3 * kPBox;       // two weight boxes + 128 token rows
-constexpr int kPStages = 4;
 constexpr int kPEpiStage = 4 * 2048;
-constexpr int kPDynSmem = kPStages * kPStageBytes + 1024 + kPEpiStage;
+constexpr int kPRing = 192 * 1024;            // stage ring per CTA
+constexpr int kPDynSmem = kPRing + 1024 + kPEpiStage;
 constexpr int kPTmemCols = 512;
+constexpr int kPMaxStages = 6;
+
+// Per launch: gate/up units hold two accumulators (gate, up: 2 x 256 columns = all of TMEM,
+// one buffer); down units one accumulator of 256 rows (128 per CTA), double-buffered, so
+// the MMA of the next unit overlaps the epilogue of the last and twice as many units
+// spread the down launch over the pairs in smaller waves.
+template <int kPhase>
+struct PairShape {
+  static constexpr int kAccs = kPhase == 1 ? 2 : 1;        // weight boxes / accumulators per unit
+  static constexpr int kBufs = kPhase == 1 ? 1 : 2;        // TMEM buffers
+  static constexpr int kStageBytes = (kAccs + 1) * kPBox;  // weight boxes + 128 token rows
+  static constexpr int kStages = kPRing / kStageBytes;     // 4 / 6
+  static_assert(kStages <= kPMaxStages, "stage barriers");
+};
 
 __device__ __forceinline__ void pair_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -78,8 +95,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     ffn_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_tok,
                     const FfnArgs args) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  using St = PairShape<kPhase>;
+  constexpr int kStages = St::kStages;
+  constexpr int kStageBytes = St::kStageBytes;
   extern __shared__ uint8_t dyn_smem[];
-  __shared__ uint64_t full_bar[kPStages], empty_bar[kPStages], tfull_bar, tempty_bar;
+  __shared__ uint64_t full_bar[kPMaxStages], empty_bar[kPMaxStages], tfull_bar[2], tempty_bar[2];
   __shared__ uint32_t s_tmem;
   __shared__ int s_touched[kMaxExperts];
   __shared__ int s_page[kMaxExperts];
@@ -99,12 +119,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int s = 0; s < kPStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&tfull_bar, 1);
-    mbar_init(&tempty_bar, 2);  // one arrival from each CTA's epilogue
+    for (int b = 0; b < St::kBufs; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2);  // one arrival from each CTA's epilogue
+    }
     fence_mbarrier_init();
   }
   if (threadIdx.x == 32) prefetch_tmap(&tm_w), prefetch_tmap(&tm_tok);
@@ -165,8 +187,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
   const int ntouched = s_ntouched;
   const int tiles = s_ntp[ntouched];
-  // phase 1: 256 features per pair unit; phase 2: 512 rows of w2 per pair unit, split-K
-  const int mt_n = kPhase == 1 ? (I + 255) / 256 : (H + 511) / 512;
+  // phase 1: 256 features per pair unit; phase 2: 256 rows of w2 per pair unit, split-K
+  const int mt_n = kPhase == 1 ? (I + 255) / 256 : (H + 255) / 256;
   const int S = kPhase == 1 ? 1 : args.splits;
   const int kbt = (kPhase == 1 ? H : I) / kPBK;
   const int total = tiles * mt_n * S;
@@ -231,23 +253,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const int nb = (nlen + 31) & ~31;
         const int page = s_page[un.te];
         const int rA0 = kPhase == 1 ? page * 3 * I + un.mt * 256 + static_cast<int>(rank) * 128
-                                    : page * 3 * H + 2 * H + un.mt * 512 + static_cast<int>(rank) * 128;
-        const int rA1 = kPhase == 1 ? rA0 + I : rA0 + 256;
+                                    : page * 3 * H + 2 * H + un.mt * 256 + static_cast<int>(rank) * 128;
+        const int rA1 = rA0 + I;  // up rows (gate/up units only)
         const int rB = row0 + n0 + static_cast<int>(rank) * (nb / 2);
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], ph ^ 1u, args.status, &s_abort)) {
             ok = false;
             break;
           }
-          uint8_t* st = ring + stage * kPStageBytes;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * kPStageBytes);
+          uint8_t* st = ring + stage * kStageBytes;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * kStageBytes);
           const uint32_t bar = map_shared_rank(smem_u32(&full_bar[stage]), 0);
           tma_load_2d_pair(st, &tm_w, bar, kb * kPBK, rA0, pol_w);
-          tma_load_2d_pair(st + kPBox, &tm_w, bar, kb * kPBK, rA1, pol_w);
-          tma_load_2d_pair(st + 2 * kPBox, &tm_tok, bar, kb * kPBK, rB, pol_t);
-          tma_load_2d_pair(st + 2 * kPBox + kPBox / 2, &tm_tok, bar, kb * kPBK, rB + 64, pol_t);
+          if (St::kAccs == 2) tma_load_2d_pair(st + kPBox, &tm_w, bar, kb * kPBK, rA1, pol_w);
+          uint8_t* sb = st + St::kAccs * kPBox;
+          tma_load_2d_pair(sb, &tm_tok, bar, kb * kPBK, rB, pol_t);
+          tma_load_2d_pair(sb + kPBox / 2, &tm_tok, bar, kb * kPBK, rB + 64, pol_t);
           ++issued;
-          if (++stage == kPStages) {
+          if (++stage == kStages) {
             stage = 0;
             ph ^= 1u;
           }
@@ -255,9 +278,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       }
       // tail: every stage's last release (a commit the leader's MMA thread aims at this
       // CTA's empty barrier) has arrived before this CTA may go
-      for (int i = 0; ok && i < kPStages; ++i) {
+      for (int i = 0; ok && i < kStages; ++i) {
         if (!mbar_wait(&empty_bar[stage], ph ^ 1u, args.status, &s_abort)) break;
-        if (++stage == kPStages) {
+        if (++stage == kStages) {
           stage = 0;
           ph ^= 1u;
         }
@@ -271,69 +294,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       uint32_t ph = 0;
       int ul = 0;
       bool ok = true;
-      const uint32_t peer_tfull = map_shared_rank(smem_u32(&tfull_bar), 1);
+
       for (int u = pair; ok && u < total; u += pairs, ++ul) {
         const PairUnit un = decode(u);
         int row0, n0, nlen;
         tokens_of(un, row0, n0, nlen);
         const int nb = (nlen + 31) & ~31;
         const uint32_t idesc = idesc_f16(kBF16, 256, nb);
-        if (!mbar_wait(&tempty_bar, (ul & 1) ^ 1u, args.status, &s_abort)) break;
+        const int buf = ul % St::kBufs;
+        if (!mbar_wait(&tempty_bar[buf], ((ul / St::kBufs) & 1) ^ 1u, args.status, &s_abort)) break;
         tc_fence_after();
+        const uint32_t acc0 = tmem + static_cast<uint32_t>(buf * 256);
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], ph, args.status, &s_abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = ring_base + stage * kPStageBytes;
+          const uint32_t a = ring_base + stage * kStageBytes;
           const uint64_t ad0 = desc_kmajor_sw128(a);
           const uint64_t ad1 = desc_kmajor_sw128(a + kPBox);
-          const uint64_t bd = desc_kmajor_sw128(a + 2 * kPBox);
+          const uint64_t bd = desc_kmajor_sw128(a + St::kAccs * kPBox);
 #pragma unroll
           for (int kk = 0; kk < kPBK / 16; ++kk) {
             const uint32_t acc = (kb > un.kb0 || kk > 0) ? 1u : 0u;
-            umma_f16_pair(tmem, ad0 + 2 * kk, bd + 2 * kk, idesc, acc);
-            umma_f16_pair(tmem + 256u, ad1 + 2 * kk, bd + 2 * kk, idesc, acc);
+            umma_f16_pair(acc0, ad0 + 2 * kk, bd + 2 * kk, idesc, acc);
+            if (St::kAccs == 2) umma_f16_pair(tmem + 256u, ad1 + 2 * kk, bd + 2 * kk, idesc, acc);
           }
           // the stage is free in both CTAs once these MMAs have read it
           umma_commit_pair(smem_u32(&empty_bar[stage]));
           umma_commit_pair(map_shared_rank(smem_u32(&empty_bar[stage]), 1));
           ++consumed;
-          if (++stage == kPStages) {
+          if (++stage == kStages) {
             stage = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit_pair(smem_u32(&tfull_bar));
-        umma_commit_pair(peer_tfull);
+        umma_commit_pair(smem_u32(&tfull_bar[buf]));
+        umma_commit_pair(map_shared_rank(smem_u32(&tfull_bar[buf]), 1));
       }
-      // tail: both epilogues' last releases (one of them remote) have arrived
-      if (ok && ul > 0) mbar_wait(&tempty_bar, (ul & 1) ^ 1u, args.status, &s_abort);
+      // tail: both epilogues' last releases of every buffer (one of them remote) have arrived
+      for (int j = ul - St::kBufs; ok && j < ul; ++j) {
+        if (j >= 0) mbar_wait(&tempty_bar[j % St::kBufs], (j / St::kBufs) & 1, args.status, &s_abort);
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;            // TMEM lanes this warp may read
     const int et = threadIdx.x - 64;         // 0..127
     const uint64_t pol_keep = policy_evict_last();
-    const uint32_t tempty_leader = map_shared_rank(smem_u32(&tempty_bar), 0);
+
     uint8_t* stg = dyn_smem + (kPDynSmem - kPEpiStage) + quarter * 2048;
     int ul = 0;
     for (int u = pair; u < total; u += pairs, ++ul) {
       const PairUnit un = decode(u);
       int row0, n0, nlen;
       tokens_of(un, row0, n0, nlen);
-      if (et == 0) s_epi_ok = mbar_wait(&tfull_bar, ul & 1, args.status, &s_abort) ? 1 : 0;
+      const int buf = ul % St::kBufs;
+      if (et == 0) s_epi_ok = mbar_wait(&tfull_bar[buf], (ul / St::kBufs) & 1, args.status, &s_abort) ? 1 : 0;
       pair_bar_sync(1, 128);
       const bool ok = s_epi_ok != 0;
       pair_bar_sync(1, 128);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t lane_base = s_tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t lane_base = s_tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * 256);
       for (int c0 = 0; c0 < nlen; c0 += 16) {
         float va[16], vb[16];
-        tmem_ld16x2(lane_base + static_cast<uint32_t>(c0), lane_base + 256u + static_cast<uint32_t>(c0), va, vb);
+        if (kPhase == 1) {
+          tmem_ld16x2(lane_base + static_cast<uint32_t>(c0), lane_base + 256u + static_cast<uint32_t>(c0), va, vb);
+        } else {
+          tmem_ld16(lane_base + static_cast<uint32_t>(c0), va);
+        }
         const int nt = min(16, nlen - c0);
         if (kPhase == 1) {
           // activations of 32 features x 16 tokens through shared memory, 16-byte stores
@@ -370,14 +402,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
             __syncwarp();
           };
-          put_rows(va, un.mt * 512 + static_cast<int>(rank) * 128);
-          put_rows(vb, un.mt * 512 + 256 + static_cast<int>(rank) * 128);
+          put_rows(va, un.mt * 256 + static_cast<int>(rank) * 128);
         }
       }
       // this CTA's half of the accumulators is drained: tell the leader's MMA thread
       tc_fence_before();
       pair_bar_sync(1, 128);
-      if (et == 0) mbar_arrive_cluster(tempty_leader);
+      if (et == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&tempty_bar[buf]), 0));
     }
   }
 
