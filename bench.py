@@ -637,9 +637,12 @@ def bench_flushed_config(cfg, dev, stream, n, hbm_peak, flush_bytes: int = 256 <
 
     for _ in range(3):
         step()
-    gr = graph_of(step, dev)
+    gr, cs = graph_of(step, dev, with_stream=True)
+    ws = ops.Workspace.lookup(dev, cs)
     times = []
     for i in range(n + 3):
+        if i == 3:
+            ops.read_timers(ws, reset=True)
         scratch.fill_(i & 0xFF)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -648,13 +651,18 @@ def bench_flushed_config(cfg, dev, stream, n, hbm_peak, flush_bytes: int = 256 <
         b.synchronize()
         if i >= 3:
             times.append(a.elapsed_time(b) * 1e-3)
+    tm = ops.read_timers(ws)
     touched = touched_experts(logits, cfg.k, cfg.renormalize)
-    _, layer_b, _ = algorithmic(cfg, touched)
+    ffn_b, layer_b, _ = algorithmic(cfg, touched)
     t = statistics.median(times)
+    ffn_s = tm["ffn_ns"] / max(1, tm["ffn_launches"]) * 1e-9
+    stages = stage_means(tm, busy=True)
     del gr, pool, scratch
     return {"workload": cfg.name, "T": cfg.T, "us_per_layer": round(t * 1e6, 2),
             "tokens_per_s": round(cfg.T / t, 1), "experts_touched": touched, "alg_bytes": layer_b,
             "layer_hbm_frac": round(layer_b / t / 1e9 / hbm_peak, 4),
+            "ffn_us": round(ffn_s * 1e6, 2), "ffn_hbm_frac": round(ffn_b / ffn_s / 1e9 / hbm_peak, 4),
+            "kernel_busy_us": stages, "splits": ops.splits(cfg.E, cfg.H, cfg.I, cfg.T * cfg.k),
             "l2": f"{flush_bytes >> 20} MB buffer written before every timed replay (outside the events)",
             "timing": f"median of {n} single graph replays"}
 
