@@ -147,7 +147,7 @@ int splits_for(int E, int H, int I, int Tk, int valid, int* out) {
   const char* env = std::getenv("SMB_SPLIT_K");
   if (env != nullptr) {
     int v = std::atoi(env);
-    if (v >= 1 && v <= I / 64) s = v;
+    if (v >= 1 && v <= I / 64 && v <= kMaxSplits) s = v;
   }
   *out = s;
   return SMB_OK;

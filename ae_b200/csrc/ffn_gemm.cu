@@ -20,8 +20,11 @@
 // A phase-2 unit of expert e and split s needs the phase-1 units of e whose features lie
 // in the split's K range: phase-1 epilogues count their finished units per (expert,
 // split) (release), the token loaders of phase 2 wait for the count (acquire, bounded).
-// Units are claimed in order (all phase-1 units first) and the grid is at most one CTA
-// per SM, so the waits end.
+// On the expert side of an exchange, phase-3 (fix-up) units follow: 64 rows of H of one
+// output tile each, summed over the S splits by the loader warps once the tile's down
+// units have counted in, and written to the sources' chunks.  Units are claimed in order
+// (all phase-1 units first, fix-ups last) and the grid is at most one CTA per SM, so the
+// waits end.
 //
 // Data movement.  Each SM's TMA engine delivers about 50 GB/s; 148 SMs together
 // saturate HBM only if TMA moves nothing but weights.  So weights come by TMA in 16 KB
@@ -83,6 +86,10 @@ constexpr int kPrefetchBlocks = 16;
 // boxes) instead of cp.async: at 128+ tokens per expert the loader warps' cp.async stream
 // fell behind the MMA.  Narrower experts of the same launch keep cp.async.
 constexpr int kTmaBMin = SMB_TMA_B_MIN;            // K blocks of the first unit warmed in L2 (512 KB)
+// Fix-up units per output tile of the exchange: 32 of its 256 rows of H each, so the sums
+// of the last tiles spread over many CTAs instead of one epilogue.
+constexpr int kFixChunks = 8;
+constexpr int kFixRows = 256 / kFixChunks;
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -118,17 +125,17 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 
 struct Unit {
-  int phase;  // 1 or 2
+  int phase;  // 1 gate/up, 2 down, 3 fix-up of an output tile of the exchange
   int te;     // index into the touched-expert list
   int mt;     // 128-feature tile (phase 1) or 256-row tile of w2 (phase 2)
   int nt;     // token tile of the expert (ncap tokens each)
-  int ks;     // split index (phase 2)
+  int ks;     // split index (phase 2), 64-row chunk of the tile (phase 3)
   int kb0;    // first 64-wide K block
   int kb1;    // one past the last K block
 };
 
 struct Geometry {
-  int n1, n2, total;  // phase-1 units, phase-2 units, all
+  int n1, n2, n3, total;  // phase-1, phase-2 and phase-3 units, all
   int m1, m2;         // tiles per expert
   int kb1_total, kb2_total;
   int splits;         // down split-K factor S
@@ -147,7 +154,8 @@ __device__ __forceinline__ int expert_of_tile(const Geometry& g, int q) {
 }
 
 // Unit order: all gate/up units, expert by expert, then feature tile and token tile; then
-// all down units, expert by expert, then split, row tile and token tile.
+// all down units, expert by expert, then split, row tile and token tile; then the fix-up
+// units, expert by expert, then row tile, token tile and chunk.
 // Units that stream the same weight rows for different token tiles are adjacent, so they
 // are claimed at about the same time and the later ones read the rows from L2.
 __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
@@ -162,6 +170,19 @@ __device__ __forceinline__ Unit decode(int u, const Geometry& g) {
     r.ks = 0;
     r.kb0 = 0;
     r.kb1 = g.kb1_total;
+  } else if (u >= g.n1 + g.n2) {
+    const int per_tile = g.m2 * kFixChunks;
+    const int v0 = u - g.n1 - g.n2;
+    r.phase = 3;
+    r.te = expert_of_tile(g, v0 / per_tile);
+    const int nte = g.ntp[r.te + 1] - g.ntp[r.te];
+    const int v = v0 - g.ntp[r.te] * per_tile;
+    r.mt = v / (nte * kFixChunks);
+    const int q = v - r.mt * nte * kFixChunks;
+    r.nt = q / kFixChunks;
+    r.ks = q - r.nt * kFixChunks;
+    r.kb0 = 0;
+    r.kb1 = 0;
   } else {
     // expert-major like the gate/up units, then split: an expert's first down units read
     // only its first features, whose gate/up units finish first
@@ -219,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t dyn_smem[];
   __shared__ uint64_t fullA_bar[kMaxStages], fullB_bar[kMaxStages], empty_bar[kMaxStages];
-  __shared__ uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
+  __shared__ uint64_t tfull_bar[2], tempty_bar[2], drain_bar, fix_bar;
   __shared__ uint64_t qfull_bar[kQueue], qempty_bar[kQueue];
   __shared__ int s_queue[kQueue];
   __shared__ uint32_t s_tmem;
@@ -227,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_page[kMaxExperts];
   __shared__ int s_ntp[kMaxExperts + 1];
   __shared__ int s_ntouched, s_ncap, s_stages;
-  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_epi_last, s_issued, s_consumed, s_last_cta;
+  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed, s_last_cta;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -257,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qempty_bar[q], kQueueReaders);
     }
     mbar_init(&drain_bar, 1);
+    mbar_init(&fix_bar, kLoaderWarps);
     fence_mbarrier_init();
   }
   if (threadIdx.x == 32) {
@@ -377,7 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = s_ntp[s_ntouched];
   g.n1 = do1 ? tiles * g.m1 : 0;
   g.n2 = do2 ? tiles * g.m2 * g.splits : 0;
-  g.total = g.n1 + g.n2;
+  g.n3 = do2 && args.ep_C > 0 ? tiles * g.m2 * kFixChunks : 0;
+  g.total = g.n1 + g.n2 + g.n3;
 
   // Units are handed out dynamically: the producer claims the next unit id from a
   // global counter (zeroed by the router) and publishes it through a small queue in
@@ -410,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int qi = 0;
       uint32_t qph = 0;
       int issued = 0;
+      uint32_t fix_phase = 0;
       bool ok = true;
       while (ok) {
         if (!mbar_wait(&qempty_bar[qi], qph ^ 1u, args.status, &s_abort)) break;
@@ -423,6 +447,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (u < 0) break;
         const Unit un = decode(u, g);
+        if (un.phase == 3) {
+          // no weights: claim nothing more until the loader warps have done this fix-up,
+          // so that fix-ups spread over the CTAs instead of queueing up in one
+          if (!mbar_wait(&fix_bar, fix_phase, args.status, &s_abort)) break;
+          fix_phase ^= 1u;
+          continue;
+        }
         const int page = s_page[un.te];
         if (args.page_ready != nullptr) {
           // streamed pages: the weights of this unit's page must have arrived
@@ -480,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int u = next_unit(qi, qph);
         if (u < 0) break;
         const Unit un = decode(u, g);
+        if (un.phase == 3) continue;  // no MMA
         int row0, n0, nlen;
         tile_tokens(un, row0, n0, nlen);
         const int nb = (nlen + 15) & ~15;
@@ -549,6 +581,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = s_touched[un.te];
       int row0, n0, nlen;
       tile_tokens(un, row0, n0, nlen);
+      if (un.phase == 3) {
+        // fix-up: once all S down units of the output tile have stored their partials,
+        // sum this chunk's rows in split order and write them to the sources' chunks
+        int ready = 1;
+        if (lane == 0) {
+          ready = wait_count(args.tile_done + (e * g.m2 + un.mt) * args.ntc + un.nt, g.splits, args.status,
+                             &s_abort) ? 1 : 0;
+        }
+        ready = __shfl_sync(full, ready, 0);
+        __syncwarp();
+        if (!ready) break;
+        const int h0 = un.mt * 256 + un.ks * kFixRows;
+        const int nh4 = max(0, min(kFixRows, H - h0)) / 4;  // float4 per row of the chunk
+        const size_t sstride = static_cast<size_t>(args.Tk) * H;
+        for (int idx = bt; idx < nlen * nh4; idx += kLoaderThreads) {
+          const int r = idx / nh4, c4 = idx - r * nh4;
+          const int p = row0 + n0 + r;
+          const int h = h0 + c4 * 4;
+          const float* src = args.part + static_cast<size_t>(p) * H + h;
+          // every split's load in flight at once, then the sum in split order
+          float4 v[kMaxSplits];
+#pragma unroll
+          for (int j = 0; j < kMaxSplits; ++j) {
+            if (j < g.splits) v[j] = __ldcg(reinterpret_cast<const float4*>(src + j * sstride));
+          }
+          const int f = args.perm[p];
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int j = 0; j < kMaxSplits; ++j) {
+            if (j < g.splits) {
+              acc.x += v[j].x;
+              acc.y += v[j].y;
+              acc.z += v[j].z;
+              acc.w += v[j].w;
+            }
+          }
+          if (f < 0 || f >= args.Tk) continue;
+          const int src_rank = f / args.ep_C;
+          const int i = f - src_rank * args.ep_C;
+          union {
+            T h[4];
+            uint2 u;
+          } pk;
+          pk.h[0] = from_f32<T>(acc.x);
+          pk.h[1] = from_f32<T>(acc.y);
+          pk.h[2] = from_f32<T>(acc.z);
+          pk.h[3] = from_f32<T>(acc.w);
+          *reinterpret_cast<uint2*>(reinterpret_cast<T*>(args.link.chunk[src_rank]) + static_cast<size_t>(i) * H + h) =
+              pk.u;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&fix_bar);
+        continue;
+      }
       const int K = un.phase == 1 ? H : I;
       const int nb = (nlen + 15) & ~15;
       int ready = 1;
@@ -632,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, 128);
       if (u < 0) break;
       const Unit un = decode(u, g);
+      if (un.phase == 3) continue;  // done by the loader warps
       const int e = s_touched[un.te];
       int row0, n0, nlen;
       tile_tokens(un, row0, n0, nlen);
@@ -694,49 +781,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&tempty_bar[buf]);
       ++pass;
       if (un.phase == 2 && args.ep_C > 0) {
-        // expert side of the exchange: publish this unit's partials; the unit that
-        // completes the output tile (all S splits stored) sums them in split order and
-        // writes each row to its source's chunk in the storage dtype
+        // expert side of the exchange: publish this unit's partials (release at GPU
+        // scope) and count it for its output tile; the tile's fix-up units sum them
         __threadfence();
         named_bar_sync(1, 128);
-        if (et == 0) {
-          const int old = atomicAdd(args.tile_done + (e * g.m2 + un.mt) * args.ntc + un.nt, 1);
-          s_epi_last = old == g.splits - 1 ? 1 : 0;
-          __threadfence();
-        }
-        named_bar_sync(1, 128);
-        if (s_epi_last) {
-          const int h0 = un.mt * 256;
-          const int nh4 = min(256, H - h0) / 4;  // float4 per row of the tile
-          for (int idx = et; idx < nlen * nh4; idx += 128) {
-            const int r = idx / nh4, c4 = idx - r * nh4;
-            const int p = row0 + n0 + r;
-            const int h = h0 + c4 * 4;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp = 0; sp < g.splits; ++sp) {
-              const float4 v =
-                  __ldcg(reinterpret_cast<const float4*>(args.part + (static_cast<size_t>(sp) * args.Tk + p) * H + h));
-              acc.x += v.x;
-              acc.y += v.y;
-              acc.z += v.z;
-              acc.w += v.w;
-            }
-            const int f = args.perm[p];
-            if (f < 0 || f >= args.Tk) continue;
-            const int src = f / args.ep_C;
-            const int i = f - src * args.ep_C;
-            union {
-              T h[4];
-              uint2 u;
-            } pk;
-            pk.h[0] = from_f32<T>(acc.x);
-            pk.h[1] = from_f32<T>(acc.y);
-            pk.h[2] = from_f32<T>(acc.z);
-            pk.h[3] = from_f32<T>(acc.w);
-            *reinterpret_cast<uint2*>(reinterpret_cast<T*>(args.link.chunk[src]) + static_cast<size_t>(i) * H + h) =
-                pk.u;
-          }
-        }
+        if (et == 0) atomicAdd(args.tile_done + (e * g.m2 + un.mt) * args.ntc + un.nt, 1);
       } else if (un.phase == 1 && chained) {
         // publish: this tile's A2 columns are written (release at GPU scope); count it
         // for every down split whose K range overlaps its 128 features

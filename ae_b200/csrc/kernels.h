@@ -66,10 +66,11 @@ struct FfnArgs {
   int page_epoch;
   StageClock* clk;                // stage clock of the call's chain (stage 2), or nullptr
   // Expert side of the exchange (ep_C > 0): the down units of an output tile (256 rows of
-  // H x one token tile) count themselves in tile_done; the one that completes the tile
-  // sums its rows' S split partials in split order and writes the sums, in the storage
-  // dtype, to row f % C of chunk f / C of `link` (f = perm[p], the slot of position p).
-  // Over peer memory the grid's last CTA then raises each source's return flag.
+  // H x one token tile) count themselves in tile_done; fix-up units (64 rows of H of one
+  // such tile each, claimed after every down unit) wait for the tile's S splits, sum their
+  // rows' partials in split order and write the sums, in the storage dtype, to row f % C
+  // of chunk f / C of `link` (f = perm[p], the slot of position p).  Over peer memory the
+  // grid's last CTA then raises each source's return flag.
   int* tile_done;                 // [E*m2*ntc] finished down units per (expert, row tile, token tile)
   const int32_t* perm;            // [Tk] slot of each expert-major position
   int ep_C;                       // C, or 0: partials only (the combine kernel reduces them)

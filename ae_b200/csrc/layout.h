@@ -12,6 +12,7 @@ namespace smb {
 constexpr int kMaxExperts = 256;   // router keeps up to 8 logits per lane
 constexpr int kMaxTopK = 8;
 constexpr int kMaxFlat = 16384;    // T*k limit of the single-pass permutation
+constexpr int kMaxSplits = 16;     // down split-K factor S (the fix-up sums S partials in registers)
 constexpr size_t kAlign = 256;
 constexpr size_t kWsHeaderBytes = 256;  // status block at offset 0, zeroed by smb_moe_workspace_init
 
@@ -163,7 +164,7 @@ inline int choose_splits(int E, int H, int I, int Tk, int num_sms, int valid_tk 
   const int sms = num_sms > 0 ? num_sms : 1;
   const int m1 = (I + 127) / 128;
   const int m2 = (H + 255) / 256;
-  const int smax = kb2 < 16 ? kb2 : 16;
+  const int smax = kb2 < kMaxSplits ? kb2 : kMaxSplits;
   typedef std::priority_queue<double, std::vector<double>, std::greater<double>> Heap;
   // phase 1 is the same for every S: simulate it once
   Heap base;

@@ -1079,7 +1079,7 @@ def run_ep_rank(args, cfg, dev):
     on this GPU, with local buffers instead of peers (for profiling; no metric line): the
     dispatch of T/G tokens, the local experts on a receive buffer built from G sources'
     chunks for this rank, and the final combine, each timed from graph replays."""
-    from ae_b200 import configs
+    from ae_b200 import configs, ops
     from ae_b200.ep import CudaBackend
     G = args.ep_rank
     E_loc, T_r = cfg.E // G, cfg.T // G
@@ -1106,7 +1106,17 @@ def run_ep_rank(args, cfg, dev):
         gr = graph_of(fn, dev)
         for _ in range(3):
             gr.replay()
+        if name == "experts":
+            ws = b._bufs[("ws_exp", G, C)]
+            ops.read_timers_at(ws.data_ptr(), ws.numel(), dev, reset=True)
         res[name + "_us"] = round(timed_steps(gr.replay, args.steps, stream) / args.steps * 1e6, 2)
+        if name == "experts":
+            tm = ops.read_timers_at(ws.data_ptr(), ws.numel(), dev)
+            res["ffn_us"] = round(tm["ffn_ns"] / max(1, tm["ffn_launches"]) / 1e3, 2)
+            wbytes = E_loc * 3 * cfg.H * cfg.I * 2
+            res["ffn_hbm_frac"] = round(wbytes / (res["ffn_us"] * 1e-6) / 1e9 / peaks()[0], 4)
+    if os.environ.get("SMB_SPLIT_K"):
+        res["split_k"] = int(os.environ["SMB_SPLIT_K"])
     hdr = recv.view(G, C + 1, cfg.H)[:, 0].contiguous().view(torch.int32)[:, :E_loc]
     res["rows_received"] = int(hdr.sum())
     emit({"ep_rank_emulation": {"workload": cfg.name, "ranks": G, "experts_per_rank": E_loc, **res}})

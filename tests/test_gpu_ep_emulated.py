@@ -1,0 +1,97 @@
+"""Expert-parallel layer with G ranks emulated on one GPU, through the NCCL-style entry
+points (``smb_moe_ep_dispatch`` / ``smb_moe_ep_experts`` / ``smb_moe_ep_combine``).
+
+Each emulated rank has its own backend (buffers, workspaces) and its E/G experts' pages;
+the exchange is done by copying chunks between the ranks' buffers, in the layout the
+all-to-all moves: source s's send chunk d becomes destination d's receive chunk s, and
+destination d's output chunk s becomes source s's returned chunk d.  Every rank's output
+is checked against the fp32 CPU oracle of the whole layer on that rank's tokens
+(``oracle.stack_fused_moe``), its routing ids bit-exact.  The expert side exercises the
+FFN kernel's exchange output (split-K fix-up units writing the returned rows), also at
+the full Mixtral-8x7B expert size with one expert per rank (S = 9) and with S forced to
+16 (two batches of loads per fix-up row).
+"""
+import os
+
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+
+def _emulate(G, E, k, H, I, tokens, pool_full, xs, logits):
+    from ae_b200.ep import CudaBackend
+    dev = pool_full.device
+    E_loc = E // G
+    C = max(1, max(tokens)) * k
+    backs = [CudaBackend(E, k, H, I, torch.bfloat16, dev) for _ in range(G)]
+    sends, states = [], []
+    for r in range(G):
+        send, state = backs[r].dispatch(xs[r], logits[r], G, C)
+        sends.append(send.clone())
+        states.append(state)
+    outs = []
+    for d in range(G):
+        recv = torch.cat([sends[s][d * (C + 1):(d + 1) * (C + 1)] for s in range(G)])
+        pool = pool_full[d * E_loc:(d + 1) * E_loc].contiguous()
+        pages = torch.arange(E_loc, device=dev, dtype=torch.int64)
+        outs.append(backs[d].experts(recv, G, C, pool, pages, E_loc).clone())
+    res = []
+    for s in range(G):
+        back = torch.cat([outs[d][s * C:(s + 1) * C] for d in range(G)])
+        res.append(backs[s].combine(back, states[s], tokens[s], G, C).clone())
+    torch.cuda.synchronize()
+    return res
+
+
+def _check(res, E, k, pool_full, xs, logits, bar_max_abs):
+    pc = pool_full.cpu()
+    pages = torch.arange(E)
+    for r, out in enumerate(res):
+        if xs[r].shape[0] == 0:
+            assert out.shape[0] == 0
+            continue
+        w, ids = mo.select_experts(logits[r].cpu(), k, True)
+        ref = mo.stack_fused_moe(xs[r].cpu(), pc, pages, w, ids, rounding="fp32").float()
+        bar = bar_max_abs
+        if bar is None:
+            ref_r = mo.stack_fused_moe(xs[r].cpu(), pc, pages, w, ids, rounding="reference").float()
+            bar = max(2e-2, float((ref_r - ref).abs().max()))
+        max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+        print(f"PARITY emulated rank {r}/{len(res)}: max_abs={max_abs:.4e} rel_l2={rel:.4e} bar={bar:.4e}")
+        assert max_abs <= bar and rel <= 1e-2, (r, max_abs, bar, rel)
+
+
+@pytest.mark.parametrize("G,split_k", [(2, None), (4, None), (8, None), (8, 16)])
+def test_emulated_ranks_small_experts(G, split_k, monkeypatch):
+    if split_k is not None:
+        monkeypatch.setenv("SMB_SPLIT_K", str(split_k))
+    E, k, H, I = 8, 2, 1024, 3584
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11 * G)
+    pool = (torch.randn(E, 3 * I * H, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    tokens = [24 - (5 * r) % 11 for r in range(G)]
+    tokens[-1] = 0 if G > 2 else tokens[-1]  # one rank without tokens
+    xs = [torch.randn(t, H, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+    logits = [torch.randn(t, E, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+    res = _emulate(G, E, k, H, I, tokens, pool, xs, logits)
+    _check(res, E, k, pool, xs, logits, 2e-2)
+
+
+@pytest.mark.parametrize("G", [2, 8])
+def test_emulated_ranks_full_size_experts(G):
+    """Mixtral-8x7B experts, 32 tokens per rank (the C2 T=256 layer over 8 ranks)."""
+    from ae_b200 import configs
+    cfg = configs.BY_KEY["c2-256"]
+    dev = torch.device("cuda", 0)
+    pool = configs.make_pool(cfg, dev, seed=0)
+    tokens = [32] * G
+    xs, logits = [], []
+    for r in range(G):
+        x, lg = configs.make_inputs(cfg, dev, seed=r, T=32)
+        xs.append(x)
+        logits.append(lg)
+    res = _emulate(G, cfg.E, cfg.k, cfg.H, cfg.I, tokens, pool, xs, logits)
+    _check(res, cfg.E, cfg.k, pool, xs, logits, None)
