@@ -74,7 +74,7 @@ class Timers(ctypes.Structure):
                 ("stage_calls", ctypes.c_uint32 * 5), ("reserved2", ctypes.c_uint32),
                 ("stage_busy_ns", ctypes.c_uint64 * 5)]
 
-    STAGES = ("route", "recv_route", "ffn", "combine", "final_combine")
+    STAGES = ("route", "reserved", "ffn", "combine", "final_combine")
 
     def as_dict(self):
         d = {f[0]: int(getattr(self, f[0])) for f in self._fields_[:6]}

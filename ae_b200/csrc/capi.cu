@@ -256,7 +256,6 @@ int gate_grid(int T, int sms) {
 
 struct EpLayout {
   void* send = nullptr;        // dispatch mode marker (rows go to link.chunk[d])
-  const void* recv = nullptr;  // experts: tokens are the payload rows of [G][C+1][H]
   int G = 0, C = 0, Eloc = 1;
   EpLink link{};
 };
@@ -306,7 +305,7 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
              const SharedIn& shared = SharedIn()) {
   WsLayout L;
   // the expert side of the exchange: about C of its G x C slots hold a token
-  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L, ep.recv != nullptr ? ep.C : -1);
+  int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L);
   if (rc != SMB_OK) return rc;
   if (logits != nullptr && logits_dtype != SMB_DTYPE_F16 && logits_dtype != SMB_DTYPE_BF16 &&
       logits_dtype != SMB_DTYPE_F32)
@@ -314,9 +313,9 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   // over peer memory a rank without tokens still sends its (empty) chunks and flags
   if (T == 0 && !ep.link.p2p) return SMB_OK;
   if (x == nullptr && T > 0) return SMB_ERR_NULL;
-  if (T > 0 && gate == nullptr && logits == nullptr && ep.recv == nullptr && (in_w == nullptr || in_ids == nullptr))
+  if (T > 0 && gate == nullptr && logits == nullptr && (in_w == nullptr || in_ids == nullptr))
     return SMB_ERR_NULL;
-  if (gate != nullptr && (gate->weight == nullptr || ep.send != nullptr || ep.recv != nullptr)) return SMB_ERR_NULL;
+  if (gate != nullptr && (gate->weight == nullptr || ep.send != nullptr)) return SMB_ERR_NULL;
   if (!aligned(x, 16)) return SMB_ERR_ALIGN;
   if (gate != nullptr && !aligned(gate->weight, 16)) return SMB_ERR_ALIGN;
   DeviceInfo di;
@@ -348,14 +347,13 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
   a.done = at<int>(ws, L.done);
   a.done_count = L.ndone;
   a.ep_send = ep.send;
-  a.ep_recv = ep.recv;
   a.ep_G = ep.G;
   a.ep_C = ep.C;
   a.ep_Eloc = ep.Eloc;
   a.link = ep.link;
   // over peer memory the whole exchange chain stamps the arena's clock
   a.clk = ep.link.p2p ? clock_at(ep.link.ctrl) : clock_at(ws);
-  a.stage = ep.recv != nullptr ? 1 : 0;
+  a.stage = 0;
   const int Tk = T * k;
   if (gate != nullptr) {
     // gate + routing in one launch: the gate's CTAs each take ceil(T / SMs) tokens, the
@@ -400,7 +398,8 @@ bool use_pair_path(int Tk, int E, int phases, bool special) {
 int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, const int64_t* page_of_expert, int dtype,
            int T, int E, int k, int H, int I, void* ws, size_t ws_bytes, cudaStream_t stream, int phases,
            bool counters_zeroed, const int* page_ready = nullptr, int page_epoch = 0, StageClock* clk = nullptr,
-           const EpLink* out_link = nullptr) {
+           const EpLink* out_link = nullptr, int recv_G = 0, const int* recv_flags = nullptr,
+           const int* recv_epoch = nullptr) {
   WsLayout L;
   int rc = carve(ws, ws_bytes, T, E, k, H, I, dtype, &L, x_chunk > 0 ? x_chunk : -1);
   if (rc != SMB_OK) return rc;
@@ -451,6 +450,15 @@ int do_ffn(const void* x, int x_chunk, const void* pool, int64_t num_pages, cons
   args.clk = clk != nullptr ? clk : clock_at(ws);
   args.tile_done = args.done + static_cast<size_t>(E) * L.splits * L.ntc;
   args.perm = at<int32_t>(ws, L.perm);
+  args.ndone = L.ndone;
+  args.exit_ticket = at<int>(ws, L.status) + 2;
+  if (recv_G > 0) {
+    // expert side of the exchange: the kernel routes the received rows itself
+    args.recv_G = recv_G;
+    args.recv_flags = recv_flags;
+    args.recv_epoch = recv_epoch;
+    counters_zeroed = true;  // left at zero by the previous launch on this workspace
+  }
   if (out_link != nullptr) {
     // expert side of the exchange: the FFN writes the returned rows itself
     args.ep_C = x_chunk;
@@ -609,9 +617,10 @@ int smb_moe_combine_rows(const void* rows, void* out, int dtype, int T, int E, i
   if (T == 0) return SMB_OK;
   if (rows == nullptr || out == nullptr) return SMB_ERR_NULL;
   if (!aligned(rows, 16) || !aligned(out, 16)) return SMB_ERR_ALIGN;
-  cudaError_t err = launch_combine_rows(rows, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
-                                        dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
-                                        pdl_enabled(), nullptr, nullptr, 0, 1, nullptr, nullptr, clock_at(ws));
+  cudaError_t err = launch_combine_rows(rows, static_cast<long long>(T) * k, at<const int32_t>(ws, L.inv),
+                                        at<const float>(ws, L.w), out, T, k, H, dtype == SMB_DTYPE_BF16,
+                                        reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), nullptr, nullptr,
+                                        clock_at(ws));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -650,22 +659,15 @@ int smb_moe_ep_experts(const void* recv, int G, int C, const void* pool, int64_t
   if (!aligned(recv, 16) || !aligned(out_rows, 16)) return SMB_ERR_ALIGN;
   const int T = G * C;  // payload rows, one slot each (k = 1)
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  EpLayout ep;
-  ep.recv = recv;
-  ep.G = G;
-  ep.C = C;
-  ep.Eloc = E_loc;
   if (G > kMaxRanks) return SMB_ERR_SHAPE;
-  int rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
-                    ws_bytes, s, ep);
-  if (rc != SMB_OK) return rc;
   EpLink link{};
   link.nranks = G;
   for (int src = 0; src < G; ++src) {
     link.chunk[src] = static_cast<uint8_t*>(out_rows) + static_cast<size_t>(src) * C * H * elem_bytes_of(dtype);
   }
+  // one launch: receive routing from the chunk headers, the FFN, the returned rows
   return do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true, nullptr,
-                0, nullptr, &link);
+                0, nullptr, &link, G);
 }
 
 size_t smb_ep_arena_bytes(int G, int C, int H, int dtype) {
@@ -755,18 +757,6 @@ int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const vo
   const int T = G * C;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const void* recv = P.arena[rank] + P.A.recv;
-  EpLayout ep;
-  ep.recv = recv;
-  ep.G = G;
-  ep.C = C;
-  ep.Eloc = E_loc;
-  ep.link.nranks = G;
-  ep.link.p2p = 1;
-  ep.link.ctrl = ep_ctrl(P, rank);
-  ep.link.wait_flags = ep_flags(P, rank);  // one flag per source
-  rc = do_route(nullptr, SMB_DTYPE_F32, nullptr, nullptr, recv, dtype, T, E_loc, 1, H, I, 0, nullptr, nullptr, ws,
-                ws_bytes, s, ep);
-  if (rc != SMB_OK) return rc;
   EpLink link{};
   link.nranks = G;
   link.p2p = 1;
@@ -775,9 +765,11 @@ int smb_moe_ep_experts_p2p(int G, int rank, int C, void* const* arenas, const vo
     link.chunk[src] = P.arena[src] + P.A.back + static_cast<size_t>(rank) * C * P.row_bytes;
     link.flag[src] = ep_flags(P, src) + kEpReturnFlags + rank;
   }
-  // the FFN kernel writes every row's output into its source's arena and raises the flags
+  // one launch: waits for the sources' flags (one per source), routes the received rows
+  // from the chunk headers, runs the FFN, writes every row's output into its source's arena
+  // and raises the return flags
   return do_ffn(recv, C, pool, num_pages, page_of_expert, dtype, T, E_loc, 1, H, I, ws, ws_bytes, s, 3, true, nullptr,
-                0, clock_at(ep_ctrl(P, rank)), &link);
+                0, clock_at(ep_ctrl(P, rank)), &link, G, ep_flags(P, rank), ep_ctrl(P, rank));
 }
 
 int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int I, int G, int rank, int C,
@@ -797,11 +789,11 @@ int smb_moe_ep_combine_p2p(void* out, int dtype, int T, int E, int k, int H, int
   link.ctrl = ep_ctrl(P, rank);
   link.wait_flags = ep_flags(P, rank) + kEpReturnFlags;  // one flag per expert rank
   // T = 0 still takes part: it waits for the returns and advances this rank's epoch
-  cudaError_t err = launch_combine_rows(P.arena[rank] + P.A.back, at<const int32_t>(ws, L.inv),
-                                        at<const float>(ws, L.w), out, T, k, H, dtype == SMB_DTYPE_BF16,
-                                        reinterpret_cast<cudaStream_t>(stream), pdl_enabled(),
-                                        at<const int32_t>(ws, L.ids), at<const int32_t>(ws, L.expert_off), C, E / G,
-                                        &link, at<int>(ws, L.status), clock_at(ep_ctrl(P, rank)));
+  // the dispatch recorded each slot's row of the returned rows [G][C] in inv
+  cudaError_t err = launch_combine_rows(P.arena[rank] + P.A.back, static_cast<long long>(G) * C,
+                                        at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
+                                        dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
+                                        pdl_enabled(), &link, at<int>(ws, L.status), clock_at(ep_ctrl(P, rank)));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 
@@ -814,10 +806,10 @@ int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, int E, int
   if (T == 0) return SMB_OK;
   if (back == nullptr || out == nullptr) return SMB_ERR_NULL;
   if (!aligned(back, 16) || !aligned(out, 16)) return SMB_ERR_ALIGN;
-  cudaError_t err = launch_combine_rows(back, at<const int32_t>(ws, L.inv), at<const float>(ws, L.w), out, T, k, H,
-                                        dtype == SMB_DTYPE_BF16, reinterpret_cast<cudaStream_t>(stream),
-                                        pdl_enabled(), at<const int32_t>(ws, L.ids),
-                                        at<const int32_t>(ws, L.expert_off), C, E / G, nullptr, nullptr,
+  // the dispatch recorded each slot's row of the returned rows [G][C] in inv
+  cudaError_t err = launch_combine_rows(back, static_cast<long long>(G) * C, at<const int32_t>(ws, L.inv),
+                                        at<const float>(ws, L.w), out, T, k, H, dtype == SMB_DTYPE_BF16,
+                                        reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), nullptr, nullptr,
                                         clock_at(ws));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
@@ -903,7 +895,7 @@ int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream) {
   if (ws == nullptr) return SMB_ERR_NULL;
   if (!aligned(ws, kAlign)) return SMB_ERR_ALIGN;
   if (ws_bytes < kWsHeaderBytes) return SMB_ERR_WORKSPACE;
-  cudaError_t err = cudaMemsetAsync(ws, 0, kWsHeaderBytes, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t err = cudaMemsetAsync(ws, 0, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SMB_OK : cuda_fail(err);
 }
 

@@ -78,80 +78,103 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   if (h4 * 4 < a.H) combine_one<TO>(a, t, h4);
 }
 
-template <typename TO>
-__device__ __forceinline__ void combine_rows_one(const void* rows_v, const int32_t* inv, const float* w, void* out_v,
-                                                 int T, int k, int H, const int32_t* ids, const int32_t* expert_off,
-                                                 int ep_C, int ep_Eloc, int t, int h4) {
-  const size_t Tk = static_cast<size_t>(T) * k;
-  const TO* rows = reinterpret_cast<const TO*>(rows_v);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < k; ++j) {
-    const size_t f = static_cast<size_t>(t) * k + j;
-    const int p = inv[f];
-    if (p < 0 || static_cast<size_t>(p) >= Tk) continue;
-    const float wj = w[f];
-    size_t row = static_cast<size_t>(p);
-    if (ep_C > 0) {
-      // returned expert outputs: chunk of the destination rank, slot within it
-      const int d = ids[f] / ep_Eloc;
-      row = static_cast<size_t>(d) * ep_C + (p - expert_off[d * ep_Eloc]);
-    }
-    union {
-      uint2 u;
-      TO h[4];
-    } v;
-    // L2 loads: over peer memory the rows were written by other GPUs while this grid ran
-    v.u = __ldcg(reinterpret_cast<const uint2*>(rows + row * H) + h4);
-    acc.x += wj * to_f32<TO>(v.h[0]);
-    acc.y += wj * to_f32<TO>(v.h[1]);
-    acc.z += wj * to_f32<TO>(v.h[2]);
-    acc.w += wj * to_f32<TO>(v.h[3]);
-  }
-  union {
-    TO h[4];
-    uint2 u;
-  } pack;
-  pack.h[0] = from_f32<TO>(acc.x);
-  pack.h[1] = from_f32<TO>(acc.y);
-  pack.h[2] = from_f32<TO>(acc.z);
-  pack.h[3] = from_f32<TO>(acc.w);
-  *reinterpret_cast<uint2*>(reinterpret_cast<TO*>(out_v) + static_cast<size_t>(t) * H + static_cast<size_t>(h4) * 4) =
-      pack.u;
-}
-
 // Weighted combine of per-slot rows: out[t, h] = sum_j w[t, j] * rows[inv[t*k+j]][h], in
-// that order in fp32, rows in the storage dtype (the expert outputs of the expert-parallel
-// path returned by the all-to-all, in dispatch order).
+// that order in fp32, rows in the storage dtype: the expert outputs of the expert-parallel
+// path returned by the exchange, where the dispatch recorded in inv each slot's row of the
+// returned rows [G][C] (rank d = expert / E_loc, row within d's chunk), or per-slot rows in
+// expert-major order, where inv holds the slot's position.
+//
+// A CTA takes a contiguous range of tokens.  The row and weight of each of its slots are
+// read before the wait for the returned rows (they depend only on this rank's own
+// routing), then each thread loads all k rows' parts of up to kCombineVec 16-byte columns of
+// a token at once, so a token costs one memory round trip.  Over peer memory thread 0 first
+// waits (bounded) for every expert rank's return flag; the grid's last CTA advances the
+// epoch (GPU scope: only this rank's kernels read it).
+constexpr int kCombineVec = 4;        // 16-byte columns per thread per pass (H <= 8192 in one)
+constexpr int kCombineSlots = 256;    // slots of a CTA's token range (the launch keeps it below)
+
 template <typename TO>
 __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(const void* rows_v, const int32_t* inv,
                                                                         const float* w, void* out_v, int T, int k,
-                                                                        int H, const int32_t* ids,
-                                                                        const int32_t* expert_off, int ep_C,
-                                                                        int ep_Eloc, const EpLink link, int* status,
-                                                                        StageClock* clk) {
-  pdl_wait_prior_grids();
-  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) stage_mark(clk, 4);
-  pdl_launch_dependents();
-  const int t = blockIdx.y;
-  const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
+                                                                        int H, long long nrows, const EpLink link,
+                                                                        int* status, StageClock* clk) {
+  __shared__ long long s_row[kCombineSlots];
+  __shared__ float s_w[kCombineSlots];
   __shared__ int s_ok, s_last;
-  if (link.p2p) {
-    // the returned rows are complete once every expert rank raised its flag to this epoch
-    if (threadIdx.x == 0) {
+  pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && threadIdx.x == 0) stage_mark(clk, 4);
+  pdl_launch_dependents();
+  const int per = (T + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int t0 = min(T, static_cast<int>(blockIdx.x) * per);
+  const int t1 = min(T, t0 + per);
+  const int nslot = min(kCombineSlots, (t1 - t0) * k);
+  for (int q = threadIdx.x; q < nslot; q += kCombineThreads) {
+    const size_t f = static_cast<size_t>(t0) * k + q;
+    const int r = inv[f];
+    const bool ok = r >= 0 && r < nrows;  // else only after a failed or skipped route
+    s_row[q] = ok ? r : -1;
+    s_w[q] = ok ? w[f] : 0.f;
+  }
+  if (threadIdx.x == 0) {
+    s_ok = 1;
+    if (link.p2p) {
+      // the returned rows are complete once every expert rank raised its flag to this epoch
       const uint64_t tw = global_timer_ns();
       s_ok = wait_flags_sys(link.wait_flags, link.nranks, link.ctrl[0] + 1) ? 1 : 0;
-      if (blockIdx.x == 0 && blockIdx.y == 0 && status != nullptr) {
+      if (blockIdx.x == 0 && status != nullptr) {
         if (!s_ok) record_status(status, kDevTimeout);
         DevTimers* tm = timers_of(status);
         add_wait_time(&tm->combine_wait_ns, &tm->combine_waits, tw);
       }
     }
-    __syncthreads();
   }
-  if (h4 * 4 < H && t < T) combine_rows_one<TO>(rows_v, inv, w, out_v, T, k, H, ids, expert_off, ep_C, ep_Eloc, t, h4);
+  __syncthreads();
+  const TO* rows = reinterpret_cast<const TO*>(rows_v);
+  TO* out = reinterpret_cast<TO*>(out_v);
+  const int nv = H / 8;  // 16-byte columns of a row
+  for (int t = t0; t < t1; ++t) {
+    const int qb = (t - t0) * k;
+    for (int c0 = 0; c0 < nv; c0 += kCombineVec * kCombineThreads) {
+      uint4 v[kCombineVec][kMaxTopK];
+#pragma unroll
+      for (int u = 0; u < kCombineVec; ++u) {
+        const int c = c0 + u * kCombineThreads + static_cast<int>(threadIdx.x);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) {
+          // L2 loads: over peer memory the rows were written by other GPUs while this grid ran
+          if (j < k && c < nv && qb + j < nslot && s_row[qb + j] >= 0)
+            v[u][j] = __ldcg(reinterpret_cast<const uint4*>(rows + s_row[qb + j] * H) + c);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCombineVec; ++u) {
+        const int c = c0 + u * kCombineThreads + static_cast<int>(threadIdx.x);
+        if (c >= nv) continue;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) {
+          if (j < k && qb + j < nslot && s_row[qb + j] >= 0) {
+            const TO* e = reinterpret_cast<const TO*>(&v[u][j]);
+            const float wj = s_w[qb + j];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += wj * to_f32<TO>(e[i]);
+          }
+        }
+        union {
+          TO h[8];
+          uint4 u4;
+        } pack;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pack.h[i] = from_f32<TO>(acc[i]);
+        reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H)[c] = pack.u4;
+      }
+    }
+  }
   if (link.p2p) {
     // every CTA has read its rows: this call is finished on this rank, advance the epoch
-    if (last_cta_of_grid(link.ctrl + 3, &s_last) && threadIdx.x == 0) {
+    if (last_cta_of_grid_gpu(link.ctrl + 3, &s_last) && threadIdx.x == 0) {
       link.ctrl[0] = link.ctrl[0] + 1;
       stage_busy(clk, 4);
     }
@@ -230,16 +253,24 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 
-cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
-                                int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids,
-                                const int32_t* expert_off, int ep_C, int ep_Eloc, const EpLink* link,
+cudaError_t launch_combine_rows(const void* rows, long long nrows, const int32_t* inv, const float* w, void* out,
+                                int T, int k, int H, bool bf16, cudaStream_t stream, bool pdl, const EpLink* link,
                                 int* status, StageClock* clk) {
   EpLink lk{};
   if (link != nullptr) lk = *link;
   const void* fn = bf16 ? reinterpret_cast<const void*>(&combine_rows_kernel<__nv_bfloat16>)
                         : reinterpret_cast<const void*>(&combine_rows_kernel<__half>);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((H / 4 + kCombineThreads - 1) / kCombineThreads, T > 0 ? T : 1);  // T = 0: flags only
+  // at most one CTA per SM while a CTA's slots fit its table; T = 0: flags only
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int grid = T < sms ? T : sms;
+  const int per_max = kCombineSlots / (k > 0 ? k : 1);  // tokens whose slots fit one CTA's table
+  const int need = (T + per_max - 1) / per_max;
+  if (grid < need) grid = need;
+  if (grid < 1) grid = 1;
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kCombineThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -248,8 +279,7 @@ cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<void**>(&rows), const_cast<int32_t**>(&inv), const_cast<float**>(&w), &out, &T,
-                    &k, &H, const_cast<int32_t**>(&ids), const_cast<int32_t**>(&expert_off), &ep_C, &ep_Eloc,
-                    &lk, &status, &clk};
+                    &k, &H, &nrows, &lk, &status, &clk};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

@@ -72,6 +72,23 @@ __device__ __forceinline__ bool last_cta_of_grid(int* ticket, int* s_flag) {
   return *s_flag != 0;
 }
 
+// last_cta_of_grid at GPU scope: for a grid whose last CTA only updates this GPU's own
+// memory (read by later kernels on the same GPU), no system-scope fence is needed.
+__device__ __forceinline__ bool last_cta_of_grid_gpu(int* ticket, int* s_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int n = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+    *s_flag = atomicAdd(ticket, 1) == n - 1 ? 1 : 0;
+    if (*s_flag) {
+      __threadfence();
+      *ticket = 0;
+    }
+  }
+  __syncthreads();
+  return *s_flag != 0;
+}
+
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }

@@ -88,7 +88,11 @@ constexpr int kPrefetchBlocks = 16;
 constexpr int kTmaBMin = SMB_TMA_B_MIN;            // K blocks of the first unit warmed in L2 (512 KB)
 // Fix-up units per output tile of the exchange: 32 of its 256 rows of H each, so the sums
 // of the last tiles spread over many CTAs instead of one epilogue.
-constexpr int kFixChunks = 8;
+#ifndef SMB_FIX_CHUNKS
+#define SMB_FIX_CHUNKS 8
+#endif
+constexpr int kFixChunks = SMB_FIX_CHUNKS;
+static_assert(256 % (4 * kFixChunks) == 0, "fix-up chunks hold whole float4 columns");
 constexpr int kFixRows = 256 / kFixChunks;
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -230,6 +234,94 @@ __device__ __forceinline__ bool wait_count(const int* p, int need, int* status, 
   }
 }
 
+// Expert side of the exchange: the receive routing, by every CTA from the G x E_loc header
+// counts of the received chunks.  Payload row i of source s belongs to the local expert
+// whose run of s's counts holds i; positions are expert-major, and inside an expert ordered
+// by source, then row (the order the generic permutation gives), so row (s, i) of expert e
+// sits at off[e] + (rows of e from sources before s) + (i - first row of e in chunk s).
+// Counts are clamped to the chunk's C rows.  Writes expert_off (every CTA the same values)
+// and inv / perm of the slots this CTA gathers.  `rs`: 4 * kMaxExperts + 1 ints of shared
+// memory (G * E_loc = E <= kMaxExperts).
+template <typename T>
+__device__ __forceinline__ void receive_routing(const FfnArgs& args, int* rs, int* s_ready) {
+  const int G = args.recv_G, C = args.x_chunk, El = args.E;
+  int* s_cnt = rs;
+  int* s_start = rs + kMaxExperts;
+  int* s_base = rs + 2 * kMaxExperts;
+  int* s_off = rs + 3 * kMaxExperts;
+  if (threadIdx.x == 0) {
+    int ready = 1;
+    // this call's status (errors are recorded only after a wait budget, long after this)
+    if (blockIdx.x == 0) args.status[0] = 0;
+    if (args.recv_flags != nullptr) {
+      const uint64_t tw = global_timer_ns();
+      ready = wait_flags_sys(args.recv_flags, G, *args.recv_epoch + 1) ? 1 : 0;
+      if (!ready) record_status(args.status, kDevTimeout);
+      if (blockIdx.x == 0) {
+        DevTimers* tm = timers_of(args.status);
+        add_wait_time(&tm->recv_wait_ns, &tm->recv_waits, tw);
+      }
+    }
+    *s_ready = ready;
+  }
+  __syncthreads();
+  const size_t row_bytes = static_cast<size_t>(args.H) * sizeof(T);
+  for (int src = threadIdx.x; src < G; src += blockDim.x) {
+    const int32_t* hdr = reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(args.x) +
+                                                          static_cast<size_t>(src) * (C + 1) * row_bytes);
+    int run = 0;
+    for (int e = 0; e < El; ++e) {
+      int c = *s_ready ? __ldcg(hdr + e) : 0;  // written by the source (another GPU over peer memory)
+      c = max(0, min(c, C - run));
+      s_cnt[src * El + e] = c;
+      s_start[src * El + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < El; e += blockDim.x) {
+    int acc = 0;
+    for (int src = 0; src < G; ++src) {
+      s_base[src * El + e] = acc;
+      acc += s_cnt[src * El + e];
+    }
+    s_off[e] = acc;  // rows of expert e, for now
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int pos = 0;
+    for (int e = 0; e < El; ++e) {
+      const int c = s_off[e];
+      s_off[e] = pos;
+      args.expert_off[e] = pos;
+      pos += c;
+    }
+    s_off[El] = pos;
+    args.expert_off[El] = pos;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * El; i += blockDim.x) s_base[i] += s_off[i % El];
+  __syncthreads();
+  // the slots this CTA gathers (the same split as the gather below)
+  const int Tk = args.Tk;
+  const int per = (Tk + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int f0 = min(Tk, static_cast<int>(blockIdx.x) * per), f1 = min(Tk, f0 + per);
+  for (int f = f0 + threadIdx.x; f < f1; f += blockDim.x) {
+    const int src = f / C, i = f - (f / C) * C;
+    int p = -1;
+    for (int e = 0; e < El; ++e) {
+      const int q = src * El + e;
+      if (i >= s_start[q] && i < s_start[q] + s_cnt[q]) {
+        p = s_base[q] + (i - s_start[q]);
+        break;
+      }
+    }
+    args.inv[f] = p;
+    if (p >= 0) args.perm[p] = f;
+  }
+  __syncthreads();
+}
+
 }  // namespace
 
 template <typename T>
@@ -248,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_page[kMaxExperts];
   __shared__ int s_ntp[kMaxExperts + 1];
   __shared__ int s_ntouched, s_ncap, s_stages;
-  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed, s_last_cta;
+  __shared__ int s_abort, s_epi_ok, s_epi_unit, s_issued, s_consumed, s_last_cta, s_recv_ready;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -316,6 +408,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait_prior_grids();
   if (threadIdx.x == 0) grid_timer_begin(timers_of(args.status));
   if (threadIdx.x == 0 && blockIdx.x == 0) stage_mark(args.clk, 2);
+  if (args.recv_G > 0) {
+    // scratch in the epilogue staging area (first used by the epilogue after its first
+    // accumulator, long after this)
+    receive_routing<T>(args, reinterpret_cast<int*>(dyn_smem + (kDynSmem - kEpiStage)), &s_recv_ready);
+  }
 
   if (threadIdx.x == 0) {
     int nt = 0, maxn = 0;
@@ -823,12 +920,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-  if (args.ep_C > 0 && args.link.p2p) {
-    // every CTA's returned rows are stored into the sources' arenas: the last CTA raises
-    // each source's return flag (also after a failed wait, so that no peer stalls)
-    if (last_cta_of_grid(args.link.ctrl + 2, &s_last_cta) && threadIdx.x == 0) {
-      const int epoch = args.link.ctrl[0] + 1;
-      for (int src = 0; src < args.link.nranks; ++src) st_release_sys(args.link.flag[src], epoch);
+  const bool ret_p2p = args.ep_C > 0 && args.link.p2p;
+  if (ret_p2p || args.recv_G > 0) {
+    // the last CTA (system scope when it raises flags) zeroes the counters for the next
+    // call when no router runs before it, and over peer memory raises each source's return
+    // flag once every CTA's returned rows are stored (also after a failed wait, so that no
+    // peer stalls)
+    const bool last = ret_p2p ? last_cta_of_grid(args.link.ctrl + 2, &s_last_cta)
+                              : last_cta_of_grid_gpu(args.exit_ticket, &s_last_cta);
+    if (last) {
+      if (args.recv_G > 0) {
+        for (int i = threadIdx.x; i < args.ndone; i += blockDim.x) args.sched[i] = 0;
+        __threadfence();
+      }
+      __syncthreads();
+      if (ret_p2p && threadIdx.x == 0) {
+        const int epoch = args.link.ctrl[0] + 1;
+        for (int src = 0; src < args.link.nranks; ++src) st_release_sys(args.link.flag[src], epoch);
+      }
     }
   }
   if (threadIdx.x == 0 && grid_timer_end(timers_of(args.status))) stage_busy(args.clk, 2);

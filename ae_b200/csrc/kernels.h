@@ -44,7 +44,7 @@ struct EpLink {
 };
 
 struct FfnArgs {
-  const int32_t* expert_off;      // [E+1]
+  int32_t* expert_off;            // [E+1]
   const int64_t* page_of_expert;  // [E]  page of each expert inside the pool
   int* status;                    // device status word
   int* done;                      // [E*S*ntc] finished gate/up tiles per (expert, down split, token tile)
@@ -52,7 +52,7 @@ struct FfnArgs {
   int ntc;                        // token-tile bound per expert (counter stride)
   const void* x;                  // token rows: the layer input [T, H], or the exchange layout
   int x_chunk;                    // 0: row t of x; C > 0: payload row t of [G][C+1][H]
-  const int32_t* inv;             // [Tk] expert-major position of each flat slot
+  int32_t* inv;                   // [Tk] expert-major position of each flat slot
   int k;                          // top-k (slot f belongs to token f / k)
   void* xp;                       // [rows, H] gathered token rows, expert-major
   void* a2;                       // [rows, I] activations, expert-major
@@ -72,9 +72,21 @@ struct FfnArgs {
   // of chunk f / C of `link` (f = perm[p], the slot of position p).  Over peer memory the
   // grid's last CTA then raises each source's return flag.
   int* tile_done;                 // [E*m2*ntc] finished down units per (expert, row tile, token tile)
-  const int32_t* perm;            // [Tk] slot of each expert-major position
+  int32_t* perm;                  // [Tk] slot of each expert-major position
   int ep_C;                       // C, or 0: partials only (the combine kernel reduces them)
   EpLink link;
+  // Receive routing inside the kernel (recv_G > 0, expert side of the exchange): x is the
+  // received [G][C+1][H] (x_chunk = C), whose header rows hold each source's counts per
+  // local expert.  Every CTA derives the expert offsets and the positions of the slots it
+  // gathers from them, after waiting (bounded) for recv_flags[0..G) >= *recv_epoch + 1 when
+  // the rows come over peer memory (recv_flags non-null).  No router runs before such a
+  // launch: the grid's last CTA leaves the ndone counters at `sched` at zero for the next
+  // call (the workspace starts zeroed, smb_moe_workspace_init).
+  int recv_G;
+  const int* recv_flags;
+  const int* recv_epoch;
+  int ndone;
+  int* exit_ticket;               // CTA ticket of the launch, 0 between launches
 };
 
 cudaError_t launch_ffn_gemm(bool bf16, int grid, cudaStream_t stream, bool pdl, const CUtensorMap& w13,
@@ -111,12 +123,22 @@ struct RouteArgs {
   // expert-parallel exchange layout: G chunks of (1 header row + C payload rows) x H; a
   // header row holds the chunk's per-local-expert counts as int32 in its first bytes
   void* ep_send;           // dispatch: gather rows into link.chunk[d] (non-null marks dispatch mode)
-  const void* ep_recv;     // receive: tokens are the payload rows, ids come from the headers
   int ep_G, ep_C, ep_Eloc;
   EpLink link;
   StageClock* clk;         // stage clock of the call's chain, or nullptr
-  int stage;               // 0 routing / dispatch, 1 expert-side receive routing
+  int stage;               // stage-clock stage (0: routing / dispatch)
 };
+
+// Expert-parallel dispatch: a CTA's token rows (slots [g0, g0 + rows_per_cta) span at
+// most (rows_per_cta + k - 2) / k + 1 tokens) are copied into shared memory at the start of
+// the kernel, while the CTA routes, if they fit in this many bytes; larger spans copy
+// straight from global memory after the routing.
+constexpr int kDispatchStageBytes = 64 * 1024;
+__host__ __device__ inline int dispatch_stage_bytes(int rows_per_cta, int k, int row_bytes) {
+  const int span = (rows_per_cta + k - 2) / k + 1;
+  const long long b = static_cast<long long>(span) * row_bytes;
+  return b <= kDispatchStageBytes ? static_cast<int>(b) : 0;
+}
 
 // Router gate fused with the routing (gate_route_kernel): logits = x W^T of
 // ReplicatedLinear(H, E, bias=False) (specmoe/models/mixtral.py:85-92,111).
@@ -151,10 +173,9 @@ cudaError_t launch_combine(const CombineArgs& a, bool bf16, cudaStream_t stream,
 
 // ep_C > 0: rows are the returned expert outputs in the exchange layout [G][C][H];
 // slot f reads row (ids[f] / ep_Eloc) * ep_C + inv[f] - expert_off[(ids[f] / ep_Eloc) * ep_Eloc]
-cudaError_t launch_combine_rows(const void* rows, const int32_t* inv, const float* w, void* out, int T, int k,
-                                int H, bool bf16, cudaStream_t stream, bool pdl, const int32_t* ids = nullptr,
-                                const int32_t* expert_off = nullptr, int ep_C = 0, int ep_Eloc = 1,
-                                const EpLink* link = nullptr, int* status = nullptr, StageClock* clk = nullptr);
+cudaError_t launch_combine_rows(const void* rows, long long nrows, const int32_t* inv, const float* w, void* out,
+                                int T, int k, int H, bool bf16, cudaStream_t stream, bool pdl, const EpLink* link,
+                                int* status, StageClock* clk);
 
 // Host helpers of the C ABI shared with the other entry-point files: record a CUDA error
 // for smb_last_cuda_error (returns SMB_ERR_CUDA), and read a device status word as an

@@ -29,8 +29,8 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Device-side timers kept in a workspace's control block at byte kTimerOffset (zeroed by
 // smb_moe_workspace_init, read and optionally cleared by smb_moe_read_timers).  The FFN
 // kernel adds, per launch, the time from the first CTA past its dependency wait to the
-// last CTA done; the expert-parallel receive router and final combine add the time
-// their flag waits took.  Nanoseconds of %globaltimer.
+// last CTA done; on the expert side of the exchange the FFN kernel, on the source side
+// the final combine, add the time their flag waits took.  Nanoseconds of %globaltimer.
 constexpr size_t kTimerOffset = 64;
 struct DevTimers {
   unsigned long long ffn_neg_t0;       // ~0 - earliest CTA start of the running FFN launch (0 = none)
@@ -50,8 +50,8 @@ static_assert(kTimerOffset + sizeof(DevTimers) <= 256, "timer block inside the c
 // block 0 of each kernel, once past its wait on the previous kernel, charges the time
 // since the previous kernel's stamp to that kernel's stage and stamps itself.  Kernels of
 // a chain run one after another, so plain loads and stores suffice.  Stages: 0 routing
-// (or the expert-parallel dispatch), 1 expert-side receive routing, 2 FFN, 3 combine (the
-// expert-side combine of the exchange), 4 source-side final combine.  The last stage of a
+// (or the expert-parallel dispatch), 1 unused (reserved), 2 FFN (on the expert side of the
+// exchange with the receive routing), 3 combine, 4 source-side final combine.  The last stage of a
 // call is charged when the next call starts.
 constexpr int kStages = 5;
 constexpr size_t kStageOffset = kTimerOffset + sizeof(DevTimers);

@@ -30,6 +30,13 @@ constexpr int kRouteThreads = 512;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
 
+// Dynamic shared memory of route_body: ids, positions and weights of the Tk slots, the
+// per-warp histograms and the expert offsets.
+__host__ __device__ inline size_t route_body_smem(int T, int E, int k) {
+  const size_t Tk = static_cast<size_t>(T) * k;
+  return sizeof(int32_t) * (3 * Tk + static_cast<size_t>(kRouteWarps) * E + E + 1);
+}
+
 // L2 loads (ld.global.cg): in the gated launch the logits were written by other CTAs of
 // the same grid, so the SM's L1 must not serve them.
 template <typename TL>
@@ -148,9 +155,12 @@ __device__ __forceinline__ void route_dispatch(const void* logits, int t_begin, 
 
 // Routing + permutation of every flat slot by one CTA's worth of threads.  `cta` is the
 // index of the calling CTA among `ncta` that run the body redundantly (each writes the
-// outputs of its own flat range; CTA 0 also the offsets, headers and counters).
+// outputs of its own flat range; CTA 0 also the offsets, headers and counters).  `stage`:
+// shared memory for the token rows of this CTA's flat range in the expert-parallel dispatch
+// (copied in while the CTA routes), or nullptr.
 template <typename TL>
-__device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, int cta, int32_t* sm) {
+__device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, int cta, int32_t* sm,
+                                           uint4* stage = nullptr) {
   const int Tk = a.T * a.k;
   const int E = a.E;
   int32_t* s_ids = sm;                                   // [Tk]
@@ -167,6 +177,18 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   if (tid == 0) {
     s_bad = 0;
     if (cta == 0 && a.status != nullptr) a.status[0] = 0;
+  }
+  const int g0 = min(Tk, cta * a.rows_per_cta);
+  const int g1 = min(Tk, g0 + a.rows_per_cta);
+  if (stage != nullptr && g1 > g0) {
+    // the rows this CTA sends do not depend on the routing: start their copy now
+    const int t_first = g0 / a.k, t_last = (g1 - 1) / a.k;
+    const int n = (t_last - t_first + 1) * vec_per_row;
+    const uint4* xsrc = reinterpret_cast<const uint4*>(a.x) + static_cast<size_t>(t_first) * vec_per_row;
+    for (int i = tid; i < n; i += kRouteThreads) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(stage + i)), "l"(xsrc + i)
+                   : "memory");
+    }
   }
   __syncthreads();
 
@@ -293,12 +315,14 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
       for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
     }
   }
-  const int g0 = min(Tk, cta * a.rows_per_cta);
-  const int g1 = min(Tk, g0 + a.rows_per_cta);
   for (int f = g0 + tid; f < g1; f += kRouteThreads) {
     const int p = s_pos[f];
     if (p >= 0) a.perm[p] = f;
-    a.inv[f] = p;
+    // dispatch: the slot's row in the returned rows [G][C] (what the final combine reads)
+    // instead of its position
+    a.inv[f] = (a.ep_send == nullptr || p < 0)
+                   ? p
+                   : (s_ids[f] / a.ep_Eloc) * a.ep_C + (p - s_off[(s_ids[f] / a.ep_Eloc) * a.ep_Eloc]);
     a.ws_w[f] = s_w[f];
     a.ws_ids[f] = s_ids[f];
     const int t = f / a.k, j = f - (f / a.k) * a.k;
@@ -320,7 +344,19 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
                                     static_cast<size_t>(1 + p - s_off[d * a.ep_Eloc]) * row_bytes_out);
   };
   const int nvec = (g1 - g0) * vec_per_row;
-  for (int base = tid; base < nvec; base += 4 * kRouteThreads) {
+  if (stage != nullptr) {
+    // rows from shared memory (copied in during the routing); the stores go out together
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int t_first = g0 / a.k;
+    for (int f = g0; f < g1; ++f) {
+      if (s_pos[f] < 0) continue;
+      uint4* dst = dst_row(f, s_pos[f]);
+      const uint4* src = stage + (f / a.k - t_first) * vec_per_row;
+      for (int c = tid; c < vec_per_row; c += kRouteThreads) dst[c] = src[c];
+    }
+  }
+  for (int base = tid; stage == nullptr && base < nvec; base += 4 * kRouteThreads) {
     uint4 v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -351,103 +387,18 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
   }
 }
 
-// Expert side of the exchange (one CTA): the received payload slots f = s*C + i through
-// the E_loc local experts, from the G x E_loc header counts alone.  Payload row i of
-// source s belongs to the expert whose run of s's counts holds i; positions are
-// expert-major with ascending f inside an expert (sources in order, then rows), so row
-// (s, i) of expert e sits at off[e] + (rows of e from sources before s) + (i - first row
-// of e in chunk s) - the order the generic permutation gives, in one pass.  Counts are
-// clamped to the chunk's C rows.  Over peer memory the chunks are complete once every
-// source has raised its flag to this call's epoch; if one does not within the wait
-// budget, no row is taken.
-__device__ __forceinline__ void route_receive(const RouteArgs& a, int32_t* sm) {
-  const int G = a.ep_G, C = a.ep_C, El = a.ep_Eloc;
-  const int Tk = a.T * a.k;  // G*C slots (k = 1)
-  int32_t* s_cnt = sm;                // [G*El] rows of (source, expert)
-  int32_t* s_base = s_cnt + G * El;   // [G*El] position of the first of them
-  int32_t* s_start = s_base + G * El; // [G*El] their first row inside the source's chunk
-  int32_t* s_off = s_start + G * El;  // [El+1]
-  __shared__ int s_ready;
-  const int tid = threadIdx.x;
-  const size_t row_bytes = static_cast<size_t>(a.H) * 2;
-  if (tid == 0) {
-    if (a.status != nullptr) a.status[0] = 0;
-    s_ready = 1;
-    if (a.link.p2p) {
-      const uint64_t tw = global_timer_ns();
-      s_ready = wait_flags_sys(a.link.wait_flags, a.link.nranks, a.link.ctrl[0] + 1) ? 1 : 0;
-      if (!s_ready) record_status(a.status, kDevTimeout);
-      if (a.status != nullptr) {
-        DevTimers* tm = timers_of(a.status);
-        add_wait_time(&tm->recv_wait_ns, &tm->recv_waits, tw);
-      }
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < G * El; i += kRouteThreads) {
-    const int src = i / El, e = i - (i / El) * El;
-    const int32_t* hdr = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(a.ep_recv) +
-                                                          static_cast<size_t>(src) * (C + 1) * row_bytes);
-    s_cnt[i] = s_ready ? __ldcg(hdr + e) : 0;  // written by the source GPU while this grid waited
-  }
-  __syncthreads();
-  if (tid == 0) {
-    for (int src = 0; src < G; ++src) {
-      int run = 0;
-      for (int e = 0; e < El; ++e) {
-        int c = s_cnt[src * El + e];
-        c = max(0, min(c, C - run));
-        s_cnt[src * El + e] = c;
-        s_start[src * El + e] = run;
-        run += c;
-      }
-    }
-    int pos = 0;
-    for (int e = 0; e < El; ++e) {
-      s_off[e] = pos;
-      for (int src = 0; src < G; ++src) {
-        s_base[src * El + e] = pos;
-        pos += s_cnt[src * El + e];
-      }
-    }
-    s_off[El] = pos;
-  }
-  __syncthreads();
-  for (int e = tid; e <= El; e += kRouteThreads) a.expert_off[e] = s_off[e];
-  if (a.done != nullptr) {
-    for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
-  }
-  for (int f = tid; f < Tk; f += kRouteThreads) {
-    const int src = f / C, i = f - (f / C) * C;
-    int id = -1, p = -1;
-    for (int e = 0; e < El; ++e) {
-      const int q = src * El + e;
-      if (i >= s_start[q] && i < s_start[q] + s_cnt[q]) {
-        id = e;
-        p = s_base[q] + (i - s_start[q]);
-        break;
-      }
-    }
-    if (p >= 0) a.perm[p] = f;
-    a.inv[f] = p;
-    a.ws_w[f] = 1.0f;
-    a.ws_ids[f] = id;
-  }
-  __syncthreads();
-  if (tid == 0) stage_busy(a.clk, a.stage);
-}
-
 template <typename TL>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a, int vec_per_row) {
   extern __shared__ int32_t sm[];
   pdl_wait_prior_grids();
   if (blockIdx.x == 0 && threadIdx.x == 0) stage_mark(a.clk, a.stage);
   pdl_launch_dependents();
-  if (a.ep_recv != nullptr && a.ep_send == nullptr) {
-    route_receive(a, sm);
-    return;
+  uint4* stage = nullptr;
+  if (a.ep_send != nullptr && dispatch_stage_bytes(a.rows_per_cta, a.k, vec_per_row * 16) > 0) {
+    const size_t off = (route_body_smem(a.T, a.E, a.k) + 15) & ~static_cast<size_t>(15);
+    stage = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm) + off);
   }
-  route_body<TL>(a, vec_per_row, static_cast<int>(blockIdx.x), sm);
+  route_body<TL>(a, vec_per_row, static_cast<int>(blockIdx.x), sm, stage);
   if (gridDim.x == 1) {
     __syncthreads();
     if (threadIdx.x == 0) stage_busy(a.clk, a.stage);
@@ -601,10 +552,7 @@ cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int 
   return cudaGetLastError();
 }
 
-size_t route_smem_bytes(int T, int E, int k) {
-  const size_t Tk = static_cast<size_t>(T) * k;
-  return sizeof(int32_t) * (3 * Tk + static_cast<size_t>(kRouteWarps) * E + E + 1);
-}
+size_t route_smem_bytes(int T, int E, int k) { return route_body_smem(T, E, k); }
 
 cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStream_t stream, bool pdl) {
   static std::atomic<int> seen[3][64];
@@ -615,10 +563,14 @@ cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStrea
     case SMB_DTYPE_BF16: fn = reinterpret_cast<const void*>(&route_kernel<__nv_bfloat16>); which = 1; break;
     default: fn = reinterpret_cast<const void*>(&route_kernel<float>); which = 2; break;
   }
-  const size_t smem = route_smem_bytes(a.T, a.E, a.k);
+  int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * elem_bytes / 16);
+  size_t smem = route_smem_bytes(a.T, a.E, a.k);
+  if (a.ep_send != nullptr) {
+    const int st = dispatch_stage_bytes(a.rows_per_cta, a.k, vec_per_row * 16);
+    if (st > 0) smem = ((smem + 15) & ~static_cast<size_t>(15)) + st;
+  }
   cudaError_t err = smem > 40 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[which], 64) : cudaSuccess;
   if (err != cudaSuccess) return err;
-  int vec_per_row = static_cast<int>(static_cast<size_t>(a.H) * elem_bytes / 16);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kRouteThreads);

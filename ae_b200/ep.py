@@ -279,8 +279,8 @@ class ExpertParallelMoE:
 
     def timers(self, reset: bool = False) -> dict:
         """This rank's device-side timers (``smb_moe_read_timers``) over the calls so far:
-        the local FFN kernel launches and, over peer memory, the time the receive router
-        waited for the sources' rows and the final combine for the returned rows."""
+        the local FFN kernel launches and, over peer memory, the time the FFN kernel waited
+        for the sources' rows and the final combine for the returned rows."""
         from . import ops
         out = {}
         for key, buf in self.backend._bufs.items():

@@ -23,7 +23,9 @@ Extra keys: roofline (dominant kernel = the fused expert-FFN kernel, HBM bound),
 cpu_baseline (the CPU oracle port of the reference's arithmetic on this host), e2e
 (FusedMoE.forward with host inputs copied in and the output copied out every step),
 clocks, gpu_launches, kernels_us (per-kernel µs from a staged pass), sweep (other verify
-batch sizes), c1_flushed (C1 with the L2 flushed), c5_single_gpu, and further blocks.
+batch sizes), c1_flushed (C1 with the L2 flushed), c5_single_gpu, prefill_t2048 (the
+prefill-sized call on the CTA-pair path against the measured bf16 GEMM peaks), and further
+blocks.
 
 ``--impl reference``: rank 0 times the reference's arithmetic on the host cores (the
 reference has no CPU expert path of its own; its Triton GPU kernel is the GPU side), the
@@ -497,6 +499,11 @@ def run_ours(args, cfg, rank, world, dev):
     if not args.no_sweep:
         c5 = bench_single_config(configs.BY_KEY["c5"], dev, stream, max(10, args.steps // 2), hbm_peak)
 
+    # prefill-sized call (survey row f4): C2 at T = 2048 on the CTA-pair path
+    prefill = None
+    if not args.no_sweep:
+        prefill = bench_prefill_config(configs.BY_KEY["c2-2048"], dev, stream, max(40, args.steps), args.no_parity)
+
     # the fine-grained configuration with a shared expert (60 routed experts of I 1408,
     # top-4, shared expert I 5632 as 4 pseudo-experts in the same launch, Zipf routing)
     fine = None
@@ -578,6 +585,7 @@ def run_ours(args, cfg, rank, world, dev):
         "sweep": sweep,
         "c1_flushed": c1,
         "c5_single_gpu": c5,
+        "prefill_t2048": prefill,
         "gated_block": gated,
         "shared_expert_config": fine,
         "verify_32_layers": verify,
@@ -619,6 +627,65 @@ def bench_single_config(cfg, dev, stream, n, hbm_peak):
             "ffn_us": round(ffn_s * 1e6, 2), "ffn_hbm_frac": round(ffn_b / ffn_s / 1e9 / hbm_peak, 4),
             "splits": ops.splits(cfg.E, cfg.H, cfg.I, cfg.T * cfg.k),
             "api": "ae_b200.ops.moe_forward (smb_moe_forward)", "timing": f"{n} graph replays"}
+
+
+def bench_prefill_config(cfg, dev, stream, n, no_parity=False):
+    """Prefill-sized layer call (C2 at T = 2048: 256 routed slots per expert on average, the
+    CTA-pair path with the 2-SM MMA): graph replays after a soak of the same replays, TFLOP/s
+    of the layer and of the FFN kernel's device timer against the measured bf16 GEMM peaks
+    (sustained: a kernel timed inside a long, power-capped loop, like this one), and the
+    output checked against the fp32 CPU oracle."""
+    from ae_b200 import configs, ops
+    pool = configs.make_pool(cfg, dev, seed=0)
+    pages = torch.arange(cfg.E, device=dev, dtype=torch.int64)
+    x, logits = configs.make_inputs(cfg, dev, seed=0)
+    out = torch.empty_like(x)
+    ids = torch.empty(cfg.T, cfg.k, dtype=torch.int32, device=dev)
+
+    def step():
+        ops.moe_forward(x, logits, pool, pages, cfg.k, cfg.renormalize, out=out, topk_ids=ids)
+
+    for _ in range(3):
+        step()
+    gr, cs = graph_of(step, dev, with_stream=True)
+    ws = ops.Workspace.lookup(dev, cs)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    t_soak = time.time()
+    while time.time() < t_soak + 1.5:
+        timed_steps(gr.replay, 10, stream)
+    ops.read_timers(ws, reset=True)
+    el = timed_steps(gr.replay, n, stream)
+    t1w = time.time()
+    tm = ops.read_timers(ws)
+    time.sleep(0.15)
+    clocks = sampler.summary(t_soak + 0.5, t1w + 0.1)  # the settled part of the soak and the timed replays
+    sampler.stop()
+    _, _, flops = algorithmic(cfg, cfg.E)
+    t = el / n
+    ffn_s = tm["ffn_ns"] / max(1, tm["ffn_launches"]) * 1e-9
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        sus, burst, kind = float(pk["bf16_tflops_sustained"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        sus, burst, kind = 1400.0, 1590.0, "fallback"
+    res = {"workload": cfg.name, "T": cfg.T, "path": "CTA pairs (tcgen05.mma.cta_group::2), two launches",
+           "us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(cfg.T / t, 1),
+           "layer_tflops": round(flops / t / 1e12, 1), "ffn_us": round(ffn_s * 1e6, 2),
+           "ffn_tflops": round(flops / ffn_s / 1e12, 1),
+           "frac_of_sustained_bf16_peak": {"layer": round(flops / t / 1e12 / sus, 4),
+                                           "ffn": round(flops / ffn_s / 1e12 / sus, 4)},
+           "frac_of_burst_bf16_peak": {"layer": round(flops / t / 1e12 / burst, 4),
+                                       "ffn": round(flops / ffn_s / 1e12 / burst, 4)},
+           "peaks_tflops": {"sustained": sus, "burst": burst, "kind": kind},
+           "clocks": clocks, "timing": f"{n} graph replays after a 1.5 s soak of the same replays (clocks: soak and timed replays)",
+           "api": "ae_b200.ops.moe_forward (smb_moe_forward)"}
+    if not no_parity:
+        res["parity"] = parity_vs_oracle(out, x, logits, pool.cpu(), pages, cfg.k, cfg.renormalize, ids=ids)
+    del gr, pool
+    torch.cuda.empty_cache()
+    return res
 
 
 def bench_flushed_config(cfg, dev, stream, n, hbm_peak, flush_bytes: int = 256 << 20):
@@ -803,7 +870,7 @@ def bench_verify_step(dev, stream, hbm_peak, steps: int = 5):
     return out
 
 
-EP_STAGES = ("route", "recv_route", "ffn", "final_combine")
+EP_STAGES = ("route", "ffn", "final_combine")
 
 
 def ep_time(moe, x, logits, dev, stream, steps, soak=0.0):
@@ -1040,7 +1107,7 @@ def run_ep(args, cfg, rank, world, dev):
                 "d2h_bytes_per_step": world * x.numel() * x.element_size(),
                 "api": f"ae_b200.ep.ExpertParallelMoE.forward (transport={args.ep_transport})"},
         f"{other}_transport_us_per_layer": round(t2 / args.steps * 1e6, 2),
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 3 * args.steps,
         "clocks": clocks,
         "c5_expert_parallel": c5,
     }

@@ -185,8 +185,11 @@ SMB_API int smb_moe_ep_combine(const void* back, void* out, int dtype, int T, in
  *   experts: waits (bounded) for the G flags, runs the local experts, writes each row's
  *     output into its source's arena and raises a flag there;
  *   combine: waits (bounded) for the G return flags, weighted sum into out [T,H].
- * The experts call is two kernels (receive routing from the header counts, then the FFN,
- * whose last CTA raises the return flags), so a layer call is four kernels per rank.
+ * The experts call is one kernel (the FFN kernel routes the received rows itself from the
+ * chunks' header counts and its last CTA raises the return flags), so a layer call is
+ * three kernels per rank.  The experts workspace must start zeroed (smb_moe_workspace_init)
+ * and serve only experts calls: with no router before it, that kernel leaves its counters
+ * at zero for the next call.
  * Flags carry an epoch kept in the arena (the count of finished calls), so calls can be
  * replayed from a CUDA graph.  A wait that runs out (2 s) records SMB_ERR_DEVICE_TIMEOUT in
  * the workspace status (smb_moe_read_status) and the call continues without the missing
@@ -262,9 +265,10 @@ SMB_API int smb_moe_forward_streamed(const void* x, const void* router_logits, i
                                      void* out, float* topk_weights, int32_t* topk_ids, void* ws, size_t ws_bytes,
                                      smb_stream_t stream);
 
-/* Zero the workspace's control block (its first 256 bytes).  Call once after allocating
- * a workspace, before its first smb_moe_forward_gated call: the gated launch counts its
- * CTAs in a ticket kept there, and every call leaves the ticket at 0 again. */
+/* Zero the whole workspace (its control block, timers and counters).  Call once after
+ * allocating a workspace, before its first smb_moe_forward_gated or expert-parallel experts
+ * call: the gated launch counts its CTAs in a ticket kept in the control block, the experts
+ * call relies on zeroed counters, and every call leaves them at zero again. */
 SMB_API int smb_moe_workspace_init(void* ws, size_t ws_bytes, smb_stream_t stream);
 
 /* Router gate only: router_logits [T,E] = x [T,H] gate_weight[E,H]^T, fp32 accumulation,
@@ -325,18 +329,19 @@ SMB_API int smb_moe_read_status(const void* ws, size_t ws_bytes, int T, int E, i
  * timed from the host, specmoe/optimizer/performance_simulator/operators/gpu_fused_moe.py:84-116).
  *   ffn_ns / ffn_launches: per FFN kernel launch, from the first CTA past its wait on the
  *     router to the last CTA done, summed;
- *   recv_wait_ns / recv_waits: expert side of the peer-memory exchange, time the receive
- *     router waited for the sources' flags;
+ *   recv_wait_ns / recv_waits: expert side of the peer-memory exchange, time the FFN kernel
+ *     waited for the sources' flags;
  *   combine_wait_ns / combine_waits: source side, time the final combine waited for the
  *     returned rows;
  *   stage_ns[i] / stage_calls[i]: per stage of a layer call, from the stage's first kernel
  *     block passing its wait on the previous kernel to the next stage's; stages 0 routing
- *     (expert-parallel: dispatch), 1 expert-side receive routing, 2 FFN (expert-parallel:
- *     with the returned rows written), 3 combine, 4 source-side final combine; the last stage
+ *     (expert-parallel: dispatch), 1 unused (reserved), 2 FFN (expert-parallel: with the
+ *     wait for the sources' rows, their routing and the returned rows written), 3 combine,
+ *     4 source-side final combine; the last stage
  *     of a call ends when the next call starts; stage_busy_ns[i]: the part of it until the
  *     stage's kernel finished (recorded by its last CTA where the kernel keeps a CTA
- *     ticket: the gated or single-CTA routing, the dispatch and receive routing over peer
- *     memory, the FFN, the final combine over peer memory).  Over peer memory the whole chain keeps
+ *     ticket: the gated or single-CTA routing, the dispatch over peer memory, the FFN, the
+ *     final combine over peer memory).  Over peer memory the whole chain keeps
  *     its stage clock in the rank's exchange arena: pass the arena (its own, at least 256
  *     bytes) as `ws` to read it.
  * Reads synchronously on `stream`; reset != 0 then zeroes the timers (stream-ordered). */

@@ -11,7 +11,6 @@ FFN kernel's exchange output (split-K fix-up units writing the returned rows), a
 the full Mixtral-8x7B expert size with one expert per rank (S = 9) and with S forced to
 16 (two batches of loads per fix-up row).
 """
-import os
 
 import pytest
 import torch
@@ -21,12 +20,13 @@ from oracle import moe_oracle as mo
 pytestmark = pytest.mark.gpu
 
 
-def _emulate(G, E, k, H, I, tokens, pool_full, xs, logits):
+def _emulate(G, E, k, H, I, tokens, pool_full, xs, logits, backs=None, C=None):
     from ae_b200.ep import CudaBackend
     dev = pool_full.device
     E_loc = E // G
-    C = max(1, max(tokens)) * k
-    backs = [CudaBackend(E, k, H, I, torch.bfloat16, dev) for _ in range(G)]
+    C = C or max(1, max(tokens)) * k
+    if backs is None:
+        backs = [CudaBackend(E, k, H, I, torch.bfloat16, dev) for _ in range(G)]
     sends, states = [], []
     for r in range(G):
         send, state = backs[r].dispatch(xs[r], logits[r], G, C)
@@ -66,18 +66,24 @@ def _check(res, E, k, pool_full, xs, logits, bar_max_abs):
 
 @pytest.mark.parametrize("G,split_k", [(2, None), (4, None), (8, None), (8, 16)])
 def test_emulated_ranks_small_experts(G, split_k, monkeypatch):
+    """Three calls on the same buffers (the expert side leaves its counters at zero for the
+    next call), uneven token counts, a rank without tokens in the first call."""
+    from ae_b200.ep import CudaBackend
     if split_k is not None:
         monkeypatch.setenv("SMB_SPLIT_K", str(split_k))
     E, k, H, I = 8, 2, 1024, 3584
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(11 * G)
     pool = (torch.randn(E, 3 * I * H, generator=g, device=dev) * 0.03).to(torch.bfloat16)
-    tokens = [24 - (5 * r) % 11 for r in range(G)]
-    tokens[-1] = 0 if G > 2 else tokens[-1]  # one rank without tokens
-    xs = [torch.randn(t, H, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
-    logits = [torch.randn(t, E, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
-    res = _emulate(G, E, k, H, I, tokens, pool, xs, logits)
-    _check(res, E, k, pool, xs, logits, 2e-2)
+    backs = [CudaBackend(E, k, H, I, torch.bfloat16, dev) for _ in range(G)]
+    for call in range(3):
+        tokens = [24 - (5 * r + 3 * call) % 11 for r in range(G)]
+        if call == 0 and G > 2:
+            tokens[-1] = 0  # one rank without tokens
+        xs = [torch.randn(t, H, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+        logits = [torch.randn(t, E, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+        res = _emulate(G, E, k, H, I, tokens, pool, xs, logits, backs=backs, C=24 * k)
+        _check(res, E, k, pool, xs, logits, 2e-2)
 
 
 @pytest.mark.parametrize("G", [2, 8])
@@ -95,3 +101,28 @@ def test_emulated_ranks_full_size_experts(G):
         logits.append(lg)
     res = _emulate(G, cfg.E, cfg.k, cfg.H, cfg.I, tokens, pool, xs, logits)
     _check(res, cfg.E, cfg.k, pool, xs, logits, None)
+
+
+@pytest.mark.parametrize("T,k,H", [(37, 2, 1024), (300, 2, 4096), (5, 8, 512)])
+def test_combine_rows_expert_major(T, k, H):
+    """smb_moe_combine_rows (the same kernel as the exchange's final combine) on per-slot
+    rows in expert-major order: out[t] = sum_j w[t, j] * rows[inv[t*k + j]], fp32 sums in
+    slot order, checked against torch in fp32."""
+    from ae_b200 import ops
+    dev = torch.device("cuda", 0)
+    E, I = 16, 256
+    g = torch.Generator(device=dev).manual_seed(T * k)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev).to(torch.bfloat16)
+    L = ops.StagedLayer(T, E, k, H, I, torch.bfloat16, dev)
+    L.route(logits, x, True)
+    rows = torch.randn(T * k, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    L.combine_rows(rows, out)
+    torch.cuda.synchronize()
+    v = L.views()
+    inv = v["inv"].long()
+    w = v["w"].float()
+    ref = (rows.float()[inv].view(T, k, H) * w.view(T, k, 1)).sum(1)
+    assert L.status() == 0
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)

@@ -141,7 +141,7 @@ def test_device_timers_count_the_calls():
     # combine three times (the fourth call's combine ends no stage yet)
     assert tm["stage_calls"]["route"] == 4 and tm["stage_calls"]["ffn"] == 4
     assert tm["stage_calls"]["combine"] == 3
-    assert tm["stage_calls"]["recv_route"] == 0 and tm["stage_calls"]["final_combine"] == 0
+    assert tm["stage_calls"]["reserved"] == 0 and tm["stage_calls"]["final_combine"] == 0
     ffn_stage = tm["stage_ns"]["ffn"] / 4
     ffn_kernel = tm["ffn_ns"] / 4
     assert ffn_kernel <= ffn_stage * 1.05 + 2000, (ffn_kernel, ffn_stage)
