@@ -53,20 +53,20 @@ __device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, int epoc
 
 // Called by every thread of every CTA once its global / peer stores are issued: true in
 // the CTA that finished last; that CTA leaves the ticket at 0 for the next launch.  After
-// the CTA barrier one thread fences at system scope (cumulative over the stores of the
-// CTA it has synchronised with) and takes the ticket; in the last CTA that thread fences
-// again, so when it then raises flags every CTA's stores are visible system-wide.  Only
-// thread 0 of the last CTA may raise flags.  No CTA waits for another.
+// the CTA barrier one thread takes the ticket with an acquire-release atomic at system
+// scope: its release half is cumulative over the stores of the CTA it has synchronised
+// with, and in the last CTA its acquire half (it reads every earlier CTA's increment) orders
+// all CTAs' stores before what that thread writes next, so the flags it then raises with
+// st.release.sys publish every CTA's stores system-wide.  Only thread 0 of the last CTA may
+// raise flags.  No CTA waits for another.
 __device__ __forceinline__ bool last_cta_of_grid(int* ticket, int* s_flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
     const int n = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
-    *s_flag = atomicAdd(ticket, 1) == n - 1 ? 1 : 0;
-    if (*s_flag) {
-      __threadfence_system();
-      *ticket = 0;
-    }
+    int old;
+    asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+    *s_flag = old == n - 1 ? 1 : 0;
+    if (*s_flag) *ticket = 0;
   }
   __syncthreads();
   return *s_flag != 0;
