@@ -39,16 +39,37 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait, bounded, until flags[0..n) are all >= epoch (called by one thread).
+// Raise n flags (typically in other GPUs' memory) to v as one release: one release fence,
+// then relaxed system-scope stores that are all in flight together.  A release store per
+// flag would wait, each, for the previous flag's store to reach its GPU.
+__device__ __forceinline__ void raise_flags_sys(int* const* flags, int n, int v) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int i = 0; i < n; ++i) asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(flags[i]), "r"(v) : "memory");
+}
+
+// Wait, bounded, until flags[0..n) are all >= epoch (called by one thread; n <= kMaxRanks).
+// Each round reads every flag with relaxed system-scope loads that are in flight together
+// (one round trip, not n), and once all have reached the epoch one acquire fence orders
+// the caller's later reads after the writes the flags publish.
 __device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, int epoch) {
   const uint64_t t0 = global_timer_ns();
-  for (int s = 0; s < n; ++s) {
-    while (ld_acquire_sys(flags + s) < epoch) {
-      if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
-      __nanosleep(100);
+  while (true) {
+    int v[kMaxRanks];
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s) {
+      v[s] = epoch;
+      if (s < n) asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v[s]) : "l"(flags + s) : "memory");
     }
+    bool all = true;
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s) all = all && v[s] >= epoch;
+    if (all) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      return true;
+    }
+    if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
+    __nanosleep(100);
   }
-  return true;
 }
 
 // Called by every thread of every CTA once its global / peer stores are issued: true in

@@ -936,7 +936,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       if (ret_p2p && threadIdx.x == 0) {
         const int epoch = args.link.ctrl[0] + 1;
-        for (int src = 0; src < args.link.nranks; ++src) st_release_sys(args.link.flag[src], epoch);
+        raise_flags_sys(args.link.flag, args.link.nranks, epoch);
       }
     }
   }

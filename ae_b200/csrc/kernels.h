@@ -33,7 +33,6 @@ inline cudaError_t ensure_dyn_smem(const void* fn, int bytes, std::atomic<int>* 
 // flags its peers set, and the receive / return chunks.  chunk[d] is where this kernel
 // puts the rows meant for rank d; with the NCCL transport it points into the local send
 // buffer instead, and no flag is set or waited for.
-constexpr int kMaxRanks = 8;
 struct EpLink {
   void* chunk[kMaxRanks];  // per destination: base of this rank's chunk in its buffer
   int* flag[kMaxRanks];    // per destination: the flag slot this rank sets there (p2p)

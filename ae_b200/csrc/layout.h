@@ -12,7 +12,8 @@ namespace smb {
 constexpr int kMaxExperts = 256;   // router keeps up to 8 logits per lane
 constexpr int kMaxTopK = 8;
 constexpr int kMaxFlat = 16384;    // T*k limit of the single-pass permutation
-constexpr int kMaxSplits = 16;     // down split-K factor S (the fix-up sums S partials in registers)
+constexpr int kMaxSplits = 16;
+constexpr int kMaxRanks = 8;       // ranks of the expert-parallel exchange     // down split-K factor S (the fix-up sums S partials in registers)
 constexpr size_t kAlign = 256;
 constexpr size_t kWsHeaderBytes = 256;  // status block at offset 0, zeroed by smb_moe_workspace_init
 

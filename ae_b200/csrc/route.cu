@@ -381,7 +381,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, int vec_per_row, 
     __shared__ int s_last;
     if (last_cta_of_grid(a.link.ctrl + 1, &s_last) && tid == 0) {
       const int epoch = a.link.ctrl[0] + 1;
-      for (int d = 0; d < a.link.nranks; ++d) st_release_sys(a.link.flag[d], epoch);
+      raise_flags_sys(a.link.flag, a.link.nranks, epoch);
       stage_busy(a.clk, a.stage);
     }
   }
