@@ -126,3 +126,20 @@ def test_combine_rows_expert_major(T, k, H):
     ref = (rows.float()[inv].view(T, k, H) * w.view(T, k, 1)).sum(1)
     assert L.status() == 0
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
+def test_emulated_ranks_prefill_sized_dispatch():
+    """1250-1300 tokens per rank with H = 4096: a dispatch CTA's token rows no longer fit its
+    shared-memory staging (more than 64 KB), so the rows are copied straight from global
+    memory after the routing; the expert side then has 256-token tiles (TMA token tiles)."""
+    from ae_b200.ep import CudaBackend
+    E, k, H, I, G = 8, 2, 4096, 256, 2
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1300)
+    pool = (torch.randn(E, 3 * I * H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    tokens = [1300, 1250]
+    xs = [torch.randn(t, H, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+    logits = [torch.randn(t, E, generator=g, device=dev).to(torch.bfloat16) for t in tokens]
+    backs = [CudaBackend(E, k, H, I, torch.bfloat16, dev) for _ in range(G)]
+    res = _emulate(G, E, k, H, I, tokens, pool, xs, logits, backs=backs)
+    _check(res, E, k, pool, xs, logits, 2e-2)
