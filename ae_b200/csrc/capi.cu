@@ -239,10 +239,12 @@ int encode_2d_uncached(CUtensorMap* map, const void* base, int dtype, uint64_t r
 }
 
 // The router gathers token rows only into the expert-parallel send buffer; then the
-// copy is spread over CTAs (8 rows each).  Otherwise one CTA routes and permutes.
+// copy is spread over CTAs (2 rows each, at most one CTA per SM): over peer memory each
+// CTA waits at its release for its own stores to reach the other GPUs, so fewer rows per
+// CTA shorten both its stores and that wait.  Otherwise one CTA routes and permutes.
 int route_grid(int Tk, int sms, bool gathers) {
   if (!gathers) return 1;
-  int g = (Tk + 7) / 8;
+  int g = (Tk + 1) / 2;
   if (g < 1) g = 1;
   if (g > sms) g = sms;
   return g;
