@@ -376,6 +376,19 @@ int do_route(const void* logits, int logits_dtype, const float* in_w, const int3
     cudaError_t err = launch_gate_route(a, g, dtype, gate_grid(T, di.sms), stream, pdl_enabled());
     return err == cudaSuccess ? SMB_OK : cuda_fail(err);
   }
+  if (ep.send == nullptr && Tk >= kMultiRouteMinSlots) {
+    // large call: many CTAs route their own tokens and meet once on a table of counts (in
+    // the workspace's logits area, unused without the gate); ticket and generation words
+    // in the control block
+    int tpc = (T + di.sms - 1) / di.sms;
+    if (tpc < 32) tpc = 32;
+    const int grid = (T + tpc - 1) / tpc;
+    a.rows_per_cta = tpc * k;
+    int* ctrl = at<int>(ws, L.status);
+    cudaError_t err = launch_route_multi(a, tpc, grid, at<int>(ws, L.logits), ctrl + 3, ctrl + 4, stream,
+                                         pdl_enabled());
+    return err == cudaSuccess ? SMB_OK : cuda_fail(err);
+  }
   const int grid = route_grid(Tk, di.sms, ep.send != nullptr);
   a.rows_per_cta = (Tk + grid - 1) / grid;
   cudaError_t err = launch_route(a, elem_bytes_of(dtype), grid, stream, pdl_enabled());

@@ -157,6 +157,13 @@ cudaError_t launch_gate_route(const RouteArgs& a, const GateArgs& g, int dtype, 
 cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int k, int renorm, float* out_w,
                         int32_t* out_ids, cudaStream_t stream);
 cudaError_t launch_route(const RouteArgs& a, int elem_bytes, int grid, cudaStream_t stream, bool pdl);
+// The router over many CTAs for large calls (no gate, no exchange): tpc tokens per CTA,
+// hist [grid * E] int32 scratch, ticket and gen two int32 words that stay between calls
+// (ticket back at 0 after each launch, gen counting launches).
+constexpr int kMultiRouteMinSlots = 2048;
+size_t route_multi_smem_bytes(int tpc, int E, int k);
+cudaError_t launch_route_multi(const RouteArgs& a, int tpc, int grid, int* hist, int* ticket, int* gen,
+                               cudaStream_t stream, bool pdl);
 size_t route_smem_bytes(int T, int E, int k);
 
 struct CombineArgs {

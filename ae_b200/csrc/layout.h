@@ -74,6 +74,8 @@ inline int token_tile_cap(size_t Tk) { return Tk > 256 ? static_cast<int>((Tk + 
 // contiguous allocation); the library only carves it.
 struct WsLayout {
   size_t status;      // int32 [64]    [0] device status word, [1] CTA ticket of the gated router,
+                      //               [2] FFN exit ticket, [3] / [4] ticket and generation of the
+                      //               multi-CTA router,
                       //               timers from byte kTimerOffset; always at offset 0 so a buffer
                       //               reused for other shapes keeps it
   size_t expert_off;  // int32 [E+1]   exclusive prefix of tokens per expert

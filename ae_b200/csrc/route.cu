@@ -537,6 +537,195 @@ __global__ void __launch_bounds__(256) topk_kernel(const void* logits, int T, in
   });
 }
 
+
+// ---------------------------------------------------------------- multi-CTA router
+
+// Large calls (no gate, no exchange, Tk >= kMultiRouteMinSlots): the router over many
+// CTAs instead of one.  CTA c routes the contiguous tokens [c*tpc, (c+1)*tpc) and counts its
+// slots per expert into a table in the workspace; the CTA that takes the last ticket turns
+// the ncta x E counts into every CTA's first position per expert (expert-major, CTAs in flat
+// order) and the expert offsets, zeroes the FFN's counters and bumps a generation word,
+// while the others wait (bounded) for that bump.  Every CTA of the grid is resident at once
+// (at most one per SM; the FFN launched behind it starts only after all of them have
+// started), so the wait ends.  Then each CTA places its slots the way the one-CTA router
+// does (per-warp segments, match_any ranks), so the permutation is the same.
+template <typename TL>
+__global__ void __launch_bounds__(kRouteThreads) route_multi_kernel(const RouteArgs a, int tpc, int* hist,
+                                                                     int* ticket, int* gen) {
+  extern __shared__ int32_t sm[];
+  __shared__ int s_gen0, s_bad, s_last;
+  pdl_wait_prior_grids();
+  if (blockIdx.x == 0 && threadIdx.x == 0) stage_mark(a.clk, a.stage);
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = a.E, k = a.k;
+  const int cta = static_cast<int>(blockIdx.x);
+  const int t0 = min(a.T, cta * tpc), t1 = min(a.T, t0 + tpc);
+  const int fb = t0 * k, n = (t1 - t0) * k;  // this CTA's flat slots [fb, fb + n)
+  const int nmax = tpc * k;
+  int32_t* s_ids = sm;                                    // [nmax]
+  int32_t* s_pos = s_ids + nmax;                          // [nmax]
+  float* s_w = reinterpret_cast<float*>(s_pos + nmax);    // [nmax]
+  int32_t* s_cnt = reinterpret_cast<int32_t*>(s_w + nmax);  // [warps][E]
+  int32_t* s_base = s_cnt + kRouteWarps * E;              // [E]
+  if (tid == 0) {
+    s_gen0 = *reinterpret_cast<volatile int*>(gen);
+    s_bad = 0;
+    // this call's status (the other CTAs record only after the table below, which comes
+    // after every CTA, this one included, has taken its ticket)
+    if (cta == 0 && a.status != nullptr) a.status[0] = 0;
+  }
+  __syncthreads();
+
+  // 1. routing of this CTA's tokens (or the given routing), then the shared slots
+  const int Er = E - a.n_shared;
+  if (a.logits != nullptr) {
+    route_dispatch<TL>(a.logits, t0, t1, Er, a.k_routed, a.renormalize, tid, kRouteThreads,
+                       [&](int t, int j, int id, float w) {
+                         const int q = (t - t0) * k + j;
+                         s_ids[q] = id;
+                         s_w[q] = w;
+                       });
+    for (int i = tid; i < (t1 - t0) * a.n_shared; i += kRouteThreads) {
+      const int tt = i / a.n_shared, qq = i - (i / a.n_shared) * a.n_shared;
+      const int q = tt * k + a.k_routed + qq;
+      s_ids[q] = Er + qq;
+      s_w[q] = a.shared_w != nullptr ? a.shared_w[t0 + tt] : 1.0f;
+    }
+  } else {
+    for (int q = tid; q < n; q += kRouteThreads) {
+      const int f = fb + q;
+      const int t = f / k, j = f - (f / k) * k;
+      if (j < a.k_routed) {
+        int id = a.in_ids[t * a.k_routed + j];
+        if (id != -1 && (id < 0 || id >= Er)) {
+          s_bad = 1;
+          id = 0;
+        }
+        s_ids[q] = id;
+        s_w[q] = a.in_w[t * a.k_routed + j];
+      } else {
+        s_ids[q] = Er + (j - a.k_routed);
+        s_w[q] = a.shared_w != nullptr ? a.shared_w[t] : 1.0f;
+      }
+    }
+  }
+  for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] = 0;
+  __syncthreads();
+
+  // 2. per-warp histograms over contiguous segments of this CTA's slots; per expert the
+  // warps' offsets inside the CTA, and the CTA's count into the table
+  const int seg = (n + kRouteWarps - 1) / kRouteWarps;
+  const int q0 = min(n, warp * seg), q1 = min(n, q0 + seg);
+  for (int q = q0 + lane; q < q1; q += 32) {
+    if (s_ids[q] >= 0) atomicAdd(&s_cnt[warp * E + s_ids[q]], 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kRouteThreads) {
+    int run = 0;
+    for (int w = 0; w < kRouteWarps; ++w) {
+      const int c = s_cnt[w * E + e];
+      s_cnt[w * E + e] = run;
+      run += c;
+    }
+    hist[cta * E + e] = run;
+  }
+  __syncthreads();
+
+  // 3. the last CTA to take a ticket builds the table of first positions
+  if (tid == 0) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+    s_last = old == static_cast<int>(gridDim.x) - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (s_last) {
+    const int G = static_cast<int>(gridDim.x);
+    for (int e = tid; e < E; e += kRouteThreads) {
+      int tot = 0;
+      for (int c = 0; c < G; ++c) tot += __ldcg(hist + c * E + e);
+      s_base[e] = tot;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int pos = 0;
+      for (int e = 0; e < E; ++e) {
+        const int c = s_base[e];
+        s_base[e] = pos;
+        a.expert_off[e] = pos;
+        pos += c;
+      }
+      a.expert_off[E] = pos;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouteThreads) {
+      int run = s_base[e];
+      for (int c = 0; c < G; ++c) {
+        const int v = __ldcg(hist + c * E + e);
+        hist[c * E + e] = run;
+        run += v;
+      }
+    }
+    if (a.done != nullptr) {
+      for (int i = tid; i < a.done_count; i += kRouteThreads) a.done[i] = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      *ticket = 0;
+      __threadfence();
+      atomicExch(gen, s_gen0 + 1);  // after the fence: publishes the table
+    }
+  } else if (tid == 0) {
+    const uint64_t t_start = global_timer_ns();
+    while (*reinterpret_cast<volatile int*>(gen) == s_gen0) {
+      if (global_timer_ns() - t_start > kWaitBudgetNs) {
+        record_status(a.status, kDevTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kRouteThreads) s_base[e] = __ldcg(hist + cta * E + e);
+  __syncthreads();
+  if (tid == 0 && s_bad) record_status(a.status, kDevBadExpertId);
+
+  // 4. positions: the CTA's first position of the expert + the warp's offset + the rank
+  for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) s_cnt[i] += s_base[i % E];
+  __syncthreads();
+  for (int base = q0; base < q1; base += 32) {
+    const int q = base + lane;
+    const bool act = q < q1 && s_ids[q] >= 0;
+    const int e = act ? s_ids[q] : E + lane;
+    if (q < q1 && !act) s_pos[q] = -1;
+    const unsigned peers = __match_any_sync(kFull, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    const int bpos = act ? s_cnt[warp * E + e] : 0;
+    if (act) s_pos[q] = bpos + rank;
+    __syncwarp();
+    if (act && lane == leader) s_cnt[warp * E + e] = bpos + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // 5. outputs of this CTA's slots
+  for (int q = tid; q < n; q += kRouteThreads) {
+    const int f = fb + q;
+    const int p = s_pos[q];
+    if (p >= 0) a.perm[p] = f;
+    a.inv[f] = p;
+    a.ws_w[f] = s_w[q];
+    a.ws_ids[f] = s_ids[q];
+    const int t = f / k, j = f - (f / k) * k;
+    if (j < a.k_routed) {
+      if (a.out_w != nullptr) a.out_w[t * a.k_routed + j] = s_w[q];
+      if (a.out_ids != nullptr) a.out_ids[t * a.k_routed + j] = s_ids[q];
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_topk(const void* logits, int logits_dtype, int T, int E, int k, int renorm, float* out_w,
@@ -607,6 +796,39 @@ cudaError_t launch_gate_route(const RouteArgs& a, const GateArgs& g, int dtype, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* params[] = {const_cast<RouteArgs*>(&a), const_cast<GateArgs*>(&g), &vec_per_row};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+
+size_t route_multi_smem_bytes(int tpc, int E, int k) {
+  const size_t nmax = static_cast<size_t>(tpc) * k;
+  return sizeof(int32_t) * (3 * nmax + static_cast<size_t>(kRouteWarps) * E + E);
+}
+
+cudaError_t launch_route_multi(const RouteArgs& a, int tpc, int grid, int* hist, int* ticket, int* gen,
+                               cudaStream_t stream, bool pdl) {
+  static std::atomic<int> seen[3][64];
+  const void* fn = nullptr;
+  int which = 0;
+  switch (a.logits == nullptr ? SMB_DTYPE_F32 : a.logits_dtype) {
+    case SMB_DTYPE_F16: fn = reinterpret_cast<const void*>(&route_multi_kernel<__half>); which = 0; break;
+    case SMB_DTYPE_BF16: fn = reinterpret_cast<const void*>(&route_multi_kernel<__nv_bfloat16>); which = 1; break;
+    default: fn = reinterpret_cast<const void*>(&route_multi_kernel<float>); which = 2; break;
+  }
+  const size_t smem = route_multi_smem_bytes(tpc, a.E, a.k);
+  cudaError_t err = smem > 40 * 1024 ? ensure_dyn_smem(fn, static_cast<int>(smem), seen[which], 64) : cudaSuccess;
+  if (err != cudaSuccess) return err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {const_cast<RouteArgs*>(&a), &tpc, &hist, &ticket, &gen};
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 

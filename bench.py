@@ -679,6 +679,7 @@ def bench_prefill_config(cfg, dev, stream, n, no_parity=False):
            "frac_of_burst_bf16_peak": {"layer": round(flops / t / 1e12 / burst, 4),
                                        "ffn": round(flops / ffn_s / 1e12 / burst, 4)},
            "peaks_tflops": {"sustained": sus, "burst": burst, "kind": kind},
+           "stages_us": stage_means(tm), "kernel_busy_us": stage_means(tm, busy=True),
            "clocks": clocks, "timing": f"{n} graph replays after a 1.5 s soak of the same replays (clocks: soak and timed replays)",
            "api": "ae_b200.ops.moe_forward (smb_moe_forward)"}
     if not no_parity:

@@ -92,7 +92,9 @@ def test_align_block_size_random(T, E, k, block):
     assert (e.cpu().numpy() == re).all()
 
 
-@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (3, 8, 2), (32, 8, 2), (128, 60, 4), (513, 16, 3)])
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (3, 8, 2), (32, 8, 2), (128, 60, 4), (513, 16, 3),
+                                   # 2048+ slots: the router over many CTAs
+                                   (1024, 8, 2), (1500, 16, 3), (2048, 60, 4), (8192, 8, 2)])
 def test_route_permutation_bit_exact(T, E, k):
     from ae_b200.ops import StagedLayer
     H, I = 256, 128
@@ -111,6 +113,30 @@ def test_route_permutation_bit_exact(T, E, k):
     assert (v["inv"].cpu().numpy() == inv).all()
     assert (v["ids"].cpu().numpy() == rids.reshape(-1)).all()
     assert L.status() == 0
+
+
+@pytest.mark.parametrize("T,E,k", [(37, 8, 2), (1400, 16, 2)])
+def test_given_routing_permutation_bit_exact(T, E, k):
+    """smb_moe_permute (routing given, as stack_fused_moe passes it): the permutation of the
+    given ids, bit-exact against the oracle, with the one-CTA and the many-CTA router; two
+    calls in a row on one workspace (the many-CTA router's ticket and generation words)."""
+    from ae_b200.ops import StagedLayer
+    H, I = 256, 128
+    L = StagedLayer(T, E, k, H, I, torch.bfloat16, "cuda")
+    for call in range(2):
+        x, logits, pool, pages = make_layer(T, E, k, H, I, seed=T + call)
+        rw, rids = mo.select_experts(logits.cpu(), k, True)
+        w = torch.from_numpy(rw).cuda()
+        ids = torch.from_numpy(rids).cuda()
+        L.permute(w, ids, x)
+        v = L.views()
+        perm, off, inv = mo.permutation(rids, E)
+        assert (v["expert_off"].cpu().numpy() == off).all()
+        assert (v["perm"].cpu().numpy() == perm).all()
+        assert (v["inv"].cpu().numpy() == inv).all()
+        assert (v["ids"].cpu().numpy() == rids.reshape(-1)).all()
+        np.testing.assert_array_equal(v["w"].cpu().numpy(), rw.reshape(-1))
+        assert L.status() == 0
 
 
 # ------------------------------------------------------------------ expert FFN stages
