@@ -18,6 +18,76 @@ namespace {
 
 constexpr int kCombineThreads = 256;
 
+// out[t, 4 columns] in the storage dtype from the fp32 sum.
+template <typename TO>
+__device__ __forceinline__ void store4(const CombineArgs& a, int t, int h4, const float4& acc) {
+  TO* out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H;
+  union {
+    TO h[4];
+    uint2 u;
+  } pack;
+  pack.h[0] = from_f32<TO>(acc.x);
+  pack.h[1] = from_f32<TO>(acc.y);
+  pack.h[2] = from_f32<TO>(acc.z);
+  pack.h[3] = from_f32<TO>(acc.w);
+  *reinterpret_cast<uint2*>(out + static_cast<size_t>(h4) * 4) = pack.u;
+}
+
+// k <= 2 and S <= kCombineSplits (the usual top-2 layers): both slots' positions and weights
+// first, then every split partial of both slots at once, so a thread waits for two memory
+// round trips instead of two per slot; the sums run in the same order as combine_one's.
+// (A bound of 4 splits keeps the registers low enough for several CTAs per SM.)
+constexpr int kCombineSplits = 4;
+template <typename TO>
+__device__ __forceinline__ void combine_two(const CombineArgs& a, int t, int h4) {
+  const size_t Tk = static_cast<size_t>(a.T) * a.k;
+  const size_t split_stride = Tk * a.H / 4;  // float4 elements between splits
+  int p[2];
+  float wj[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    p[j] = -1;
+    wj[j] = 0.f;
+    if (j < a.k) {
+      const size_t f = static_cast<size_t>(t) * a.k + j;
+      const int pj = a.inv[f];
+      if (pj >= 0 && static_cast<size_t>(pj) < Tk) {  // else only after a failed or skipped route
+        p[j] = pj;
+        wj[j] = a.w[f];
+      }
+    }
+  }
+  float4 v[2][kCombineSplits];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float4* src = reinterpret_cast<const float4*>(a.part + static_cast<size_t>(p[j] < 0 ? 0 : p[j]) * a.H) + h4;
+#pragma unroll
+    for (int sp = 0; sp < kCombineSplits; ++sp) {
+      if (p[j] >= 0 && sp < a.splits) v[j][sp] = __ldg(src + sp * split_stride);
+    }
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    if (p[j] < 0) continue;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int sp = 0; sp < kCombineSplits; ++sp) {
+      if (sp < a.splits) {
+        s.x += v[j][sp].x;
+        s.y += v[j][sp].y;
+        s.z += v[j][sp].z;
+        s.w += v[j][sp].w;
+      }
+    }
+    acc.x += wj[j] * s.x;
+    acc.y += wj[j] * s.y;
+    acc.z += wj[j] * s.z;
+    acc.w += wj[j] * s.w;
+  }
+  store4<TO>(a, t, h4, acc);
+}
+
 template <typename TO>
 __device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4) {
   const size_t Tk = static_cast<size_t>(a.T) * a.k;
@@ -56,16 +126,7 @@ __device__ __forceinline__ void combine_one(const CombineArgs& a, int t, int h4)
     acc.z += wj * s.z;
     acc.w += wj * s.w;
   }
-  TO* out = reinterpret_cast<TO*>(a.out) + static_cast<size_t>(t) * a.H;
-  union {
-    TO h[4];
-    uint2 u;
-  } pack;
-  pack.h[0] = from_f32<TO>(acc.x);
-  pack.h[1] = from_f32<TO>(acc.y);
-  pack.h[2] = from_f32<TO>(acc.z);
-  pack.h[3] = from_f32<TO>(acc.w);
-  *reinterpret_cast<uint2*>(out + static_cast<size_t>(h4) * 4) = pack.u;
+  store4<TO>(a, t, h4, acc);
 }
 
 template <typename TO>
@@ -75,7 +136,13 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   pdl_launch_dependents();
   const int t = blockIdx.y;
   const int h4 = blockIdx.x * kCombineThreads + threadIdx.x;
-  if (h4 * 4 < a.H) combine_one<TO>(a, t, h4);
+  if (h4 * 4 < a.H) {
+    if (a.k <= 2 && a.splits <= kCombineSplits) {
+      combine_two<TO>(a, t, h4);
+    } else {
+      combine_one<TO>(a, t, h4);
+    }
+  }
 }
 
 // Weighted combine of per-slot rows: out[t, h] = sum_j w[t, j] * rows[inv[t*k+j]][h], in
