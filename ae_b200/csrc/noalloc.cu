@@ -17,8 +17,11 @@
 // again on the next call.  Make that first call on each device before any stream capture.
 //
 // All calls on a device share the one array and it keeps the last call's contents.
-// Nothing in it has to start at zero: every scratch element a kernel reads is written
-// earlier in the same call, and the first kernel resets the status word.  Calls that
+// Apart from the CTA tickets in its control block, nothing in it has to start at zero:
+// every other scratch element a kernel reads is written earlier in the same call, and the
+// first kernel resets the status word.  The tickets start at zero with the array (static
+// device memory is zero-initialised when the module loads) and every launch that takes
+// one leaves it at zero again.  Calls that
 // overlap on the GPU (different streams, or different host threads without ordering)
 // race on the array; callers must order them.  The kernels report a bad page id, a bad
 // expert id or a device wait that ran out in the array's status word, which
