@@ -68,6 +68,39 @@ def test_noalloc_matches_oracle_and_workspace_entry_point_two_calls():
         assert torch.equal(same, out), f"call {call}: differs from smb_moe_forward"
 
 
+def test_noalloc_large_batches_two_calls():
+    """Batches of 2048+ routed slots take the router over many CTAs, whose ticket and
+    generation words live in the scratch's control block: two such calls in a row (and the
+    smaller calls of the other tests before them, on the same scratch) against the oracle
+    and against smb_moe_forward."""
+    from ae_b200 import _native, ops
+    from oracle import moe_oracle as mo
+    lib = _native.load()
+    E, k, H, I = 8, 2, 512, 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)
+    pool = (torch.randn(E, 3 * I * H, generator=g, device="cuda") * 0.03).to(torch.bfloat16)
+    pages = torch.arange(E, dtype=torch.int64, device="cuda")
+    pool_cpu, pages_cpu = pool.cpu(), pages.cpu()
+    for call, (T, seed) in enumerate([(1100, 3), (1700, 4)]):
+        assert T * k >= 2048
+        x, logits = _batch(T, E, H, seed)
+        out = torch.full_like(x, float("nan"))
+        w = torch.empty(T, k, dtype=torch.float32, device="cuda")
+        ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+        rc = _noalloc(lib, x, logits, pool, pages, k, out, w, ids)
+        assert rc == 0, f"call {call}: {_native.strerror(rc)}"
+        assert lib.smb_moe_noalloc_read_status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+        rw, rids = mo.select_experts(logits.cpu(), k, True)
+        assert (ids.cpu().numpy() == rids).all(), f"call {call}: routing ids differ from the oracle"
+        ref = mo.stack_fused_moe(x.cpu(), pool_cpu, pages_cpu, rw, rids, rounding="fp32")
+        max_abs, rel = mo.error_metrics(out.float().cpu(), ref)
+        assert max_abs <= MAX_ABS and rel <= REL_L2, f"call {call}: max_abs={max_abs} rel={rel}"
+        same = ops.moe_forward(x, logits, pool, pages, k, True)
+        torch.cuda.synchronize()
+        assert torch.equal(same, out), f"call {call}: differs from smb_moe_forward"
+
+
 def test_noalloc_call_allocates_no_device_memory():
     from ae_b200 import _native
     lib = _native.load()
