@@ -94,6 +94,8 @@ constexpr int kTmaBMin = SMB_TMA_B_MIN;            // K blocks of the first unit
 constexpr int kFixChunks = SMB_FIX_CHUNKS;
 static_assert(256 % (4 * kFixChunks) == 0, "fix-up chunks hold whole float4 columns");
 constexpr int kFixRows = 256 / kFixChunks;
+// the loader warps and the epilogue warps share a fix-up unit
+constexpr int kFixThreads = 32 * kLoaderWarps + 128;
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -322,6 +324,55 @@ __device__ __forceinline__ void receive_routing(const FfnArgs& args, int* rs, in
   __syncthreads();
 }
 
+// Fix-up of one chunk (kFixRows rows of H) of an output tile of the exchange: rows
+// [p0, p0 + nlen) of the expert-major positions; every split's partial of an element loaded
+// at once, summed in split order, and the row written in the storage dtype into its
+// source's chunk.  Threads first, first + stride, ... take the elements.
+template <typename T>
+__device__ __forceinline__ void fixup_rows(const FfnArgs& args, int splits, int mt, int ks, int p0, int nlen,
+                                           int first, int stride) {
+  const int H = args.H;
+  const int h0 = mt * 256 + ks * kFixRows;
+  const int nh4 = max(0, min(kFixRows, H - h0)) / 4;  // float4 per row of the chunk
+  const size_t sstride = static_cast<size_t>(args.Tk) * H;
+  for (int idx = first; idx < nlen * nh4; idx += stride) {
+    const int r = idx / nh4, c4 = idx - r * nh4;
+    const int p = p0 + r;
+    const int h = h0 + c4 * 4;
+    const float* src = args.part + static_cast<size_t>(p) * H + h;
+    // every split's load in flight at once, then the sum in split order
+    float4 v[kMaxSplits];
+#pragma unroll
+    for (int j = 0; j < kMaxSplits; ++j) {
+      if (j < splits) v[j] = __ldcg(reinterpret_cast<const float4*>(src + j * sstride));
+    }
+    const int f = args.perm[p];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kMaxSplits; ++j) {
+      if (j < splits) {
+        acc.x += v[j].x;
+        acc.y += v[j].y;
+        acc.z += v[j].z;
+        acc.w += v[j].w;
+      }
+    }
+    if (f < 0 || f >= args.Tk) continue;
+    const int src_rank = f / args.ep_C;
+    const int i = f - src_rank * args.ep_C;
+    union {
+      T h[4];
+      uint2 u;
+    } pk;
+    pk.h[0] = from_f32<T>(acc.x);
+    pk.h[1] = from_f32<T>(acc.y);
+    pk.h[2] = from_f32<T>(acc.z);
+    pk.h[3] = from_f32<T>(acc.w);
+    *reinterpret_cast<uint2*>(reinterpret_cast<T*>(args.link.chunk[src_rank]) + static_cast<size_t>(i) * H + h) =
+        pk.u;
+  }
+}
+
 }  // namespace
 
 template <typename T>
@@ -370,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qempty_bar[q], kQueueReaders);
     }
     mbar_init(&drain_bar, 1);
-    mbar_init(&fix_bar, kLoaderWarps);
+    mbar_init(&fix_bar, kLoaderWarps + 1);
     fence_mbarrier_init();
   }
   if (threadIdx.x == 32) {
@@ -545,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (u < 0) break;
         const Unit un = decode(u, g);
         if (un.phase == 3) {
-          // no weights: claim nothing more until the loader warps have done this fix-up,
-          // so that fix-ups spread over the CTAs instead of queueing up in one
+          // no weights: claim nothing more until the loader and epilogue warps have done
+          // this fix-up, so that fix-ups spread over the CTAs instead of queueing up in one
           if (!mbar_wait(&fix_bar, fix_phase, args.status, &s_abort)) break;
           fix_phase ^= 1u;
           continue;
@@ -689,45 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ready = __shfl_sync(full, ready, 0);
         __syncwarp();
         if (!ready) break;
-        const int h0 = un.mt * 256 + un.ks * kFixRows;
-        const int nh4 = max(0, min(kFixRows, H - h0)) / 4;  // float4 per row of the chunk
-        const size_t sstride = static_cast<size_t>(args.Tk) * H;
-        for (int idx = bt; idx < nlen * nh4; idx += kLoaderThreads) {
-          const int r = idx / nh4, c4 = idx - r * nh4;
-          const int p = row0 + n0 + r;
-          const int h = h0 + c4 * 4;
-          const float* src = args.part + static_cast<size_t>(p) * H + h;
-          // every split's load in flight at once, then the sum in split order
-          float4 v[kMaxSplits];
-#pragma unroll
-          for (int j = 0; j < kMaxSplits; ++j) {
-            if (j < g.splits) v[j] = __ldcg(reinterpret_cast<const float4*>(src + j * sstride));
-          }
-          const int f = args.perm[p];
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int j = 0; j < kMaxSplits; ++j) {
-            if (j < g.splits) {
-              acc.x += v[j].x;
-              acc.y += v[j].y;
-              acc.z += v[j].z;
-              acc.w += v[j].w;
-            }
-          }
-          if (f < 0 || f >= args.Tk) continue;
-          const int src_rank = f / args.ep_C;
-          const int i = f - src_rank * args.ep_C;
-          union {
-            T h[4];
-            uint2 u;
-          } pk;
-          pk.h[0] = from_f32<T>(acc.x);
-          pk.h[1] = from_f32<T>(acc.y);
-          pk.h[2] = from_f32<T>(acc.z);
-          pk.h[3] = from_f32<T>(acc.w);
-          *reinterpret_cast<uint2*>(reinterpret_cast<T*>(args.link.chunk[src_rank]) + static_cast<size_t>(i) * H + h) =
-              pk.u;
-        }
+        fixup_rows<T>(args, g.splits, un.mt, un.ks, row0 + n0, nlen, bt, kFixThreads);
         __syncwarp();
         if (lane == 0) mbar_arrive(&fix_bar);
         continue;
@@ -815,7 +828,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, 128);
       if (u < 0) break;
       const Unit un = decode(u, g);
-      if (un.phase == 3) continue;  // done by the loader warps
+      if (un.phase == 3) {
+        // the epilogue warps' share of the fix-up (the loader warps take the rest)
+        int row0, n0, nlen;
+        tile_tokens(un, row0, n0, nlen);
+        if (et == 0) {
+          s_epi_ok = wait_count(args.tile_done + (s_touched[un.te] * g.m2 + un.mt) * args.ntc + un.nt, g.splits,
+                                args.status, &s_abort) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        ok = s_epi_ok != 0;
+        named_bar_sync(1, 128);
+        if (!ok) break;
+        fixup_rows<T>(args, g.splits, un.mt, un.ks, row0 + n0, nlen, kLoaderThreads + et, kFixThreads);
+        named_bar_sync(1, 128);
+        if (et == 0) mbar_arrive(&fix_bar);
+        continue;
+      }
       const int e = s_touched[un.te];
       int row0, n0, nlen;
       tile_tokens(un, row0, n0, nlen);
