@@ -14,7 +14,9 @@
 // for the expert-parallel dispatch: then every CTA recomputes the (cheap) routing and
 // copies its share of the token rows into the destination chunks of the exchange (a
 // local send buffer for NCCL, or the destinations' receive buffers over peer memory,
-// followed by a flag per destination).
+// followed by a flag per destination).  Calls of 2048+ slots without a gate or an exchange
+// use route_multi_kernel instead: many CTAs route their own tokens and meet once on a table
+// of per-CTA counts, giving the same permutation.
 #include <cfloat>
 #include <climits>
 
